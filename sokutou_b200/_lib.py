@@ -1,0 +1,55 @@
+"""ctypes binding of the C ABI declared in include/sokutou_b200.h.
+
+The shared library is built in-tree (python -m sokutou_b200.build) and loaded from
+sokutou_b200/lib/libsokutou_b200.so. There is no fallback: if the library is missing every op
+raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libsokutou_b200.so")
+
+SK_OK = 0
+ERRORS = {-1: "SK_ERR_INVALID_ARG", -2: "SK_ERR_UNSUPPORTED", -3: "SK_ERR_CUDA", -4: "SK_ERR_DEVICE",
+          -5: "SK_ERR_WORKSPACE"}
+DEVICE_ERRORS = {0: "SK_DEVERR_NONE", 1: "SK_DEVERR_POS_RANGE", 2: "SK_DEVERR_TIMEOUT"}
+SK_BF16, SK_F32 = 0, 1
+
+# every symbol the header declares, with (restype, argtypes)
+_P, _I, _F, _LL, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_longlong, ctypes.c_size_t
+SIGNATURES = {
+    "sk_version": (_I, []),
+    "sk_device_error": (_I, [ctypes.POINTER(ctypes.c_int), _I]),
+    "sk_dit_attention": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _LL, _LL, _I, _F, _P]),
+    "sk_dit_qkv_prologue": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
+    "sk_decode_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "sk_decode_attention": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
+}
+
+_lib = None
+
+
+class SokutouError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (loaded once). Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise SokutouError(f"native library missing: {LIB_PATH} (build it with `python -m sokutou_b200.build`)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != SK_OK:
+        raise SokutouError(f"{what} failed: {ERRORS.get(rc, rc)}")

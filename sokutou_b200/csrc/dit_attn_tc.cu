@@ -1,0 +1,466 @@
+// DiT attention, bf16 mode, on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces F.scaled_dot_product_attention(q, k, v, attn_mask=bias) at engine/fused.py:295.
+// One CTA computes a 128-row query tile of one (batch, head) against all K = Lk + S keys:
+//
+//   warp 4 (one lane)  TMA producer: Q once, then K/V tiles of 128 keys into a 2-stage ring.
+//                      Latent keys come from (B, H, Lk, hd); conditioning keys straight from their
+//                      batch-shared (S, H, hd) buffer — no per-CFG-branch copy.
+//   warp 5 (one lane)  MMA issuer: S_j = Q·K_jᵀ into one of two TMEM S buffers (128 fp32 columns
+//                      each), then O += P_j·V_j into the TMEM O accumulator (hd columns).
+//   warps 0-3          softmax: thread t owns query row t = TMEM lane t. It loads its S row
+//                      (tcgen05.ld), adds the key bias, keeps a running max in the log2 domain,
+//                      writes P_j (bf16) into a 128B-swizzled shared-memory tile for the next MMA,
+//                      and rescales O in TMEM only when its max grew by more than 2^8 (the result
+//                      is exact either way: numerator and denominator share the stale max).
+//                      Epilogue: O / l → bf16 → y (B, L, H, hd).
+//
+// Operand layouts (all 128-byte swizzled, 1024-byte aligned, as TMA writes them):
+//   Q [128 rows][hd]   K-major A of S = Q·Kᵀ      (hd split in 64-element chunks)
+//   K [128 keys][hd]   K-major B of S
+//   P [128 rows][128]  K-major A of O = P·V        (keys split in 64-element chunks)
+//   V [128 keys][hd]   MN-major B of O (hd contiguous), LBO = chunk stride, SBO = 8 rows
+// TMEM: columns [0,128) S0, [128,256) S1, [256, 256+hd) O; 512 columns allocated.
+#include <mutex>
+
+#include "sk_common.cuh"
+
+namespace sk {
+namespace dit {
+
+constexpr int kBM = 128, kBN = 128, kNST = 2, kNP = 2;
+constexpr int kThreadsTC = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
+
+template <int HD>
+struct TcLayout {
+  static constexpr int NCH = HD / 64;              // 64-element (128-byte) chunks per row
+  static constexpr int Q_BYTES = kBM * HD * 2;
+  static constexpr int KV_BYTES = kBN * HD * 2;
+  static constexpr int P_BYTES = kBM * kBN * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + kNST * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + kNST * KV_BYTES;
+  static constexpr int OFF_BIAS = OFF_P + kNP * P_BYTES;  // float [2][kBN]
+  static constexpr int OFF_BAR = OFF_BIAS + 2 * kBN * 4;
+  // barriers: q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2], o_done[2], mma_done
+  static constexpr int NBAR = 1 + 3 * kNST + 2 + 2 + 2 * kNP + 1;
+  static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_TMEM + 16;
+  static constexpr int SMEM_ALLOC = BYTES + 1024;  // slack to align the base to 1024
+  static_assert(SMEM_ALLOC <= 232448, "shared memory over the 227 KB per-CTA limit");
+};
+
+struct TcParams {
+  const void* bias;      // bf16 additive key bias or nullptr
+  long long bias_bs;     // elements between bias rows
+  void* y;               // bf16 (B, L, H, hd)
+  int H, L, Lk, S;
+  float scale_log2;      // softmax scale * log2(e)
+  int ctx_batched;       // 1: ctx map has a batch coordinate
+  int* err;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
+                   const __grid_constant__ CUtensorMap tmVc, const TcParams prm) {
+  using Ly = TcLayout<HD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + kNST;
+  uint64_t* kv_empty = v_full + kNST;
+  uint64_t* s_full = kv_empty + kNST;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* o_done = p_full + kNP;
+  uint64_t* mma_done = o_done + kNP;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::OFF_TMEM);
+  float* bias_s = reinterpret_cast<float*>(smem + Ly::OFF_BIAS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kBM;
+  const int n_lat = (prm.Lk + kBN - 1) / kBN, n_ctx = (prm.S + kBN - 1) / kBN;
+  const int ntiles = n_lat + n_ctx;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kNST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    for (int i = 0; i < kNP; ++i) {
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS0 = tmem, tO = tmem + 256;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      if (n_ctx) {
+        tma_prefetch_desc(&tmKc);
+        tma_prefetch_desc(&tmVc);
+      }
+      const int bh = b * prm.H + h;
+      mbar_arrive_expect_tx(q_full, Ly::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < Ly::NCH; ++c)
+        tma_load_3d(smem + Ly::OFF_Q + c * (kBM * 128), &tmQ, q_full, c * 64, q0, bh);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int s = j % kNST;
+        if (j >= kNST) ok = mbar_wait(&kv_empty[s], ((j / kNST) - 1) & 1, prm.err);
+        if (!ok) break;
+        uint8_t* kd = smem + Ly::OFF_K + s * Ly::KV_BYTES;
+        uint8_t* vd = smem + Ly::OFF_V + s * Ly::KV_BYTES;
+        mbar_arrive_expect_tx(&k_full[s], Ly::KV_BYTES);
+        if (j < n_lat) {
+#pragma unroll
+          for (int c = 0; c < Ly::NCH; ++c) tma_load_3d(kd + c * (kBN * 128), &tmK, &k_full[s], c * 64, j * kBN, bh);
+        } else {
+          const int jc = j - n_lat, bc = prm.ctx_batched ? b : 0;
+#pragma unroll
+          for (int c = 0; c < Ly::NCH; ++c)
+            tma_load_4d(kd + c * (kBN * 128), &tmKc, &k_full[s], c * 64, h, jc * kBN, bc);
+        }
+        mbar_arrive_expect_tx(&v_full[s], Ly::KV_BYTES);
+        if (j < n_lat) {
+#pragma unroll
+          for (int c = 0; c < Ly::NCH; ++c) tma_load_3d(vd + c * (kBN * 128), &tmV, &v_full[s], c * 64, j * kBN, bh);
+        } else {
+          const int jc = j - n_lat, bc = prm.ctx_batched ? b : 0;
+#pragma unroll
+          for (int c = 0; c < Ly::NCH; ++c)
+            tma_load_4d(vd + c * (kBN * 128), &tmVc, &v_full[s], c * 64, h, jc * kBN, bc);
+        }
+        issued = j + 1;
+      }
+      // Keep shared memory alive until every copy issued has landed (already true on the normal path).
+      mbar_wait(q_full, 0, prm.err);
+      for (int j = (issued > kNST ? issued - kNST : 0); j < issued; ++j) {
+        mbar_wait(&k_full[j % kNST], (j / kNST) & 1, prm.err);
+        mbar_wait(&v_full[j % kNST], (j / kNST) & 1, prm.err);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(kBM, kBN, 0, 0);
+      constexpr uint32_t idO = idesc_bf16_f32(kBM, HD, 0, 1);
+      const uint32_t aQ = sbase + Ly::OFF_Q, aK = sbase + Ly::OFF_K, aV = sbase + Ly::OFF_V, aP = sbase + Ly::OFF_P;
+      bool ok = mbar_wait(q_full, 0, prm.err);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % kNST, sb = j & 1;
+        if (!mbar_wait(&k_full[s], (j / kNST) & 1, prm.err)) return false;
+        if (j >= 2 && !mbar_wait(&s_free[sb], ((j - 2) >> 1) & 1, prm.err)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          const uint32_t offk = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
+          tc_mma_ss(tS0 + sb * 128, smem_desc_sw128(aQ + off, 16, 1024),
+                    smem_desc_sw128(aK + s * Ly::KV_BYTES + offk, 16, 1024), idS, kk > 0);
+        }
+        tc_commit(&s_full[sb]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        if (j + 1 < ntiles) ok = issue_s(j + 1);
+        if (!ok) break;
+        const int s = j % kNST, pb = j & 1;
+        if (!mbar_wait(&p_full[pb], (j >> 1) & 1, prm.err) || !mbar_wait(&v_full[s], (j / kNST) & 1, prm.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint32_t offp = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          tc_mma_ss(tO, smem_desc_sw128(aP + pb * Ly::P_BYTES + offp, 16, 1024),
+                    smem_desc_sw128(aV + s * Ly::KV_BYTES + kk * 2048, kBN * 128, 1024), idO, (j > 0 || kk > 0));
+        }
+        tc_commit(&o_done[pb]);
+        tc_commit(&kv_empty[s]);
+      }
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, prm.err);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warpgroup (warps 0-3)
+    const int row = threadIdx.x;  // TMEM lane == query row within the tile
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(prm.bias);
+    uint8_t* prow_base = smem + Ly::OFF_P + row * 128;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int sb = j & 1;
+      // key bias of this tile, log2 domain; -inf for keys past the end of their segment
+      {
+        int key = -1;
+        if (j < n_lat) {
+          const int kk = j * kBN + row;
+          key = kk < prm.Lk ? kk : -1;
+        } else {
+          const int kk = (j - n_lat) * kBN + row;
+          key = kk < prm.S ? prm.Lk + kk : -1;
+        }
+        float bv = -INFINITY;
+        if (key >= 0) bv = bias ? __bfloat162float(bias[(size_t)b * prm.bias_bs + key]) * kLog2e : 0.f;
+        bias_s[sb * kBN + row] = bv;
+      }
+      named_bar_sync(1, 128);
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, prm.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS0 + sb * 128 + lane_off + c * 32, x + c * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[sb]);
+      float mt = -INFINITY;
+      const float* bt = bias_s + sb * kBN;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        x[c] = fmaf(x[c], prm.scale_log2, bt[c]);
+        mt = fmaxf(mt, x[c]);
+      }
+      const float m_new = fmaxf(m_run, mt);
+      const bool want = m_new > m_run + kRescaleLog2;  // false while every key seen is masked
+      if (__any_sync(0xffffffffu, want)) {
+        // warp-uniform: every lane of the warp moves to its exact current max
+        const float alpha = (m_new == -INFINITY) ? 1.f : ex2_approx(m_run - m_new);
+        if (j > 0) {
+          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, prm.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            float ov[32];
+            tmem_ld32(tO + lane_off + c * 32, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_st32(tO + lane_off + c * 32, ov);
+          }
+          tmem_wait_st();
+        }
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      // P buffer sb was read by PV_{j-2}
+      if (j >= 2 && !mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, prm.err)) {
+        ok = false;
+        break;
+      }
+      float lsum = 0.f;
+      uint8_t* prow = prow_base + sb * Ly::P_BYTES;
+#pragma unroll
+      for (int u = 0; u < kBN / 8; ++u) {  // 16 units of 8 keys = 16 bytes
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2_approx(x[8 * u + 2 * e] - m_use);
+          const float p1 = ex2_approx(x[8 * u + 2 * e + 1] - m_use);
+          const __nv_bfloat162 pb2 = __floats2bfloat162_rn(p0, p1);
+          lsum += __low2float(pb2) + __high2float(pb2);
+          pk[e] = *reinterpret_cast<const uint32_t*>(&pb2);
+        }
+        const int chunk = u >> 3, unit = u & 7;
+        uint8_t* dst = prow + chunk * (kBM * 128) + ((unit ^ (row & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)), "r"(pk[0]), "r"(pk[1]),
+                     "r"(pk[2]), "r"(pk[3])
+                     : "memory");
+      }
+      l_run += lsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[sb]);
+    }
+    // ---- epilogue: y = O / l
+    if (ok && mbar_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, prm.err)) {
+      tc_fence_after();
+      const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
+      const int qi = q0 + row;
+      __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(prm.y) + (((size_t)b * prm.L + qi) * prm.H + h) * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float ov[32];
+        tmem_ld32(tO + lane_off + c * 32, ov);
+        tmem_wait_ld();
+        if (qi < prm.L) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 v2 = __floats2bfloat162_rn(ov[8 * u + 2 * e] * inv, ov[8 * u + 2 * e + 1] * inv);
+              pk[e] = *reinterpret_cast<const uint32_t*>(&v2);
+            }
+            *reinterpret_cast<uint4*>(yrow + c * 32 + u * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---- host ------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map, 128-byte swizzle, box = {64, box_rows...}; dims/strides innermost first.
+static bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_b,
+                     const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides_b, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int HD>
+static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const void* k_ctx, const void* v_ctx,
+                     long long ctx_bs, const TcParams& prm, int B, cudaStream_t st) {
+  using Ly = TcLayout<HD>;
+  const int H = prm.H, L = prm.L, Lk = prm.Lk, S = prm.S;
+  CUtensorMap mq, mk, mv, mkc, mvc;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)L, (cuuint64_t)B * H};
+    cuuint64_t str[2] = {(cuuint64_t)HD * 2, (cuuint64_t)L * HD * 2};
+    cuuint32_t box[3] = {64, kBM, 1};
+    if (!make_map(&mq, q, 3, dims, str, box)) return SK_ERR_CUDA;
+  }
+  if (Lk > 0) {
+    cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)Lk, (cuuint64_t)B * H};
+    cuuint64_t str[2] = {(cuuint64_t)HD * 2, (cuuint64_t)Lk * HD * 2};
+    cuuint32_t box[3] = {64, kBN, 1};
+    if (!make_map(&mk, k_lat, 3, dims, str, box) || !make_map(&mv, v_lat, 3, dims, str, box)) return SK_ERR_CUDA;
+  } else {
+    mk = mq;  // never read: no latent key tiles
+    mv = mq;
+  }
+  if (S > 0) {
+    // (batch, S, H, hd): box of kBN keys of one head; batch coordinate 0 when the rows share one buffer
+    cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)(prm.ctx_batched ? B : 1)};
+    cuuint64_t str[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2,
+                         (cuuint64_t)(prm.ctx_batched ? ctx_bs * 2 : (long long)S * H * HD * 2)};
+    cuuint32_t box[4] = {64, 1, kBN, 1};
+    if (!make_map(&mkc, k_ctx, 4, dims, str, box) || !make_map(&mvc, v_ctx, 4, dims, str, box)) return SK_ERR_CUDA;
+  } else {
+    mkc = mq;  // never read: no conditioning key tiles
+    mvc = mq;
+  }
+  const int smem = Ly::SMEM_ALLOC;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return SK_ERR_CUDA;
+    attr_done[dev] = true;
+  }
+  dim3 grid((L + kBM - 1) / kBM, H, B), block(kThreadsTC);
+  attn_tc_kernel<HD><<<grid, block, smem, st>>>(mq, mk, mv, mkc, mvc, prm);
+  return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
+}
+
+}  // namespace dit
+}  // namespace sk
+
+int sk_launch_dit_attention_f32(const float* q, const float* k_lat, const float* v_lat, const float* k_ctx,
+                                const float* v_ctx, const float* bias, float* y, int B, int H, int L, int Lk, int S,
+                                int hd, long long ctx_bs, long long bias_bs, float scale, cudaStream_t st);
+
+extern "C" int sk_dit_attention(const void* q, const void* k_lat, const void* v_lat, const void* k_ctx,
+                                const void* v_ctx, const void* key_bias, void* y, int B, int H, int L, int Lk, int S,
+                                int hd, long long ctx_batch_stride, long long bias_batch_stride, int dtype,
+                                float scale, void* stream) {
+  using namespace sk::dit;
+  if (!q || !y) return SK_ERR_INVALID_ARG;
+  if (B <= 0 || H <= 0 || L <= 0 || Lk < 0 || S < 0 || Lk + S <= 0) return SK_ERR_INVALID_ARG;
+  if (Lk > 0 && (!k_lat || !v_lat)) return SK_ERR_INVALID_ARG;
+  if (S > 0 && (!k_ctx || !v_ctx)) return SK_ERR_INVALID_ARG;
+  if (ctx_batch_stride < 0 || bias_batch_stride < 0) return SK_ERR_INVALID_ARG;
+  if (hd != 64 && hd != 128) return SK_ERR_UNSUPPORTED;
+  if (dtype != SK_BF16 && dtype != SK_F32) return SK_ERR_UNSUPPORTED;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_lat) |
+                       reinterpret_cast<uintptr_t>(v_lat) | reinterpret_cast<uintptr_t>(k_ctx) |
+                       reinterpret_cast<uintptr_t>(v_ctx) | reinterpret_cast<uintptr_t>(y);
+  if (al & 15) return SK_ERR_INVALID_ARG;
+  // a batched ctx buffer must keep 16-byte aligned rows for the tensor map
+  if (S > 0 && ctx_batch_stride != 0 && ((ctx_batch_stride * (dtype == SK_BF16 ? 2 : 4)) & 15))
+    return SK_ERR_INVALID_ARG;
+  int rc = sk_check_device();
+  if (rc != SK_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)hd);
+  if (dtype == SK_F32)
+    return sk_launch_dit_attention_f32(static_cast<const float*>(q), static_cast<const float*>(k_lat),
+                                       static_cast<const float*>(v_lat), static_cast<const float*>(k_ctx),
+                                       static_cast<const float*>(v_ctx), static_cast<const float*>(key_bias),
+                                       static_cast<float*>(y), B, H, L, Lk, S, hd, ctx_batch_stride,
+                                       bias_batch_stride, sc, st);
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
+  TcParams prm{key_bias, bias_batch_stride, y, H, L, Lk, S, sc * kLog2e, ctx_batch_stride != 0 ? 1 : 0, err};
+  return hd == 64 ? launch_tc<64>(q, k_lat, v_lat, k_ctx, v_ctx, ctx_batch_stride, prm, B, st)
+                  : launch_tc<128>(q, k_lat, v_lat, k_ctx, v_ctx, ctx_batch_stride, prm, B, st);
+}

@@ -1,0 +1,186 @@
+"""Torch-facing ops over the C ABI. Every call launches on torch's current CUDA stream, allocates
+only its output (and nothing when `out=` is given), and raises on any error status.
+
+DiT (engine/fused.py:293-298):
+    dit_qkv_prologue  — the `qkv` producer (engine/fused.py:117-180) without the per-batch ctx copy
+    dit_attention     — the attention over [latent | ctx] keys, y in (B, L, H, hd)
+    sdpa              — drop-in for F.scaled_dot_product_attention(q, k, v, attn_mask=bias)
+Qwen3 talker (qwen3/kernels.py:622-624):
+    decode_attention  — one layer's decode step with the reference kernel's argument list
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import SK_BF16, SK_F32, check, lib
+
+
+def _ptr(t: torch.Tensor | None) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return SK_BF16
+    if dt == torch.float32:
+        return SK_F32
+    raise TypeError(f"unsupported dtype {dt}: bfloat16 or float32")
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _cuda_contig(name: str, t: torch.Tensor) -> None:
+    _need(t.is_cuda, f"{name} must be a CUDA tensor")
+    _need(t.is_contiguous(), f"{name} must be contiguous")
+
+
+def device_error(reset: bool = True) -> int:
+    """The device error word of the current device (0 = none); synchronises the device."""
+    code = ctypes.c_int(0)
+    check(lib().sk_device_error(ctypes.byref(code), int(reset)), "sk_device_error")
+    return code.value
+
+
+# ---- DiT ----------------------------------------------------------------------------------------
+
+def dit_qkv_prologue(o4: torch.Tensor, qk_w: torch.Tensor, freqs: torch.Tensor, B: int, L: int, H: int, hd: int,
+                     eps: float, out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None):
+    """q, k_lat, v_lat (each (B, H, L, hd), o4's dtype) from o4 (B*L, 4*H*hd) = [q | k | v | gate].
+
+    qk_w: float32 (2, H, hd) q_norm/k_norm weights; freqs: float32 (>= L, hd/2, 2) RoPE (cos, sin).
+    """
+    for n, t in (("o4", o4), ("qk_w", qk_w), ("freqs", freqs)):
+        _cuda_contig(n, t)
+    _need(o4.shape == (B * L, 4 * H * hd), f"o4 must be ({B * L}, {4 * H * hd}), got {tuple(o4.shape)}")
+    _need(qk_w.dtype == torch.float32 and qk_w.numel() == 2 * H * hd, "qk_w must be float32 (2, H, hd)")
+    _need(freqs.dtype == torch.float32 and freqs.shape[0] >= L and freqs.shape[1:] == (hd // 2, 2),
+          "freqs must be float32 (>= L, hd/2, 2)")
+    if out is None:
+        out = tuple(torch.empty((B, H, L, hd), device=o4.device, dtype=o4.dtype) for _ in range(3))
+    q, k, v = out
+    for n, t in (("q", q), ("k_lat", k), ("v_lat", v)):
+        _cuda_contig(n, t)
+        _need(t.shape == (B, H, L, hd) and t.dtype == o4.dtype, f"{n} must be ({B}, {H}, {L}, {hd}) {o4.dtype}")
+    check(lib().sk_dit_qkv_prologue(_ptr(o4), _ptr(qk_w), _ptr(freqs), _ptr(q), _ptr(k), _ptr(v), B, L, H, hd,
+                                    float(eps), _dtype_code(o4.dtype), _stream()), "sk_dit_qkv_prologue")
+    return q, k, v
+
+
+def dit_attention(q: torch.Tensor, k_lat: torch.Tensor, v_lat: torch.Tensor, k_ctx: torch.Tensor | None = None,
+                  v_ctx: torch.Tensor | None = None, bias: torch.Tensor | None = None, scale: float | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(q·kᵀ·scale + bias)·v over keys [latent | ctx]; returns y (B, L, H, hd).
+
+    q: (B, H, L, hd); k_lat/v_lat: (B, H, Lk, hd); k_ctx/v_ctx: (S, H, hd) shared by every batch row,
+    or (B, S, H, hd) per row; bias: additive (K,) shared or (B, K) / (B, 1, 1, K) per row, q's dtype.
+    bfloat16 runs on the tensor cores, float32 on the fp32 CUDA-core kernel.
+    """
+    _cuda_contig("q", q)
+    B, H, L, hd = q.shape
+    dt = q.dtype
+    _cuda_contig("k_lat", k_lat)
+    _cuda_contig("v_lat", v_lat)
+    _need(k_lat.shape == v_lat.shape and k_lat.shape[:2] == (B, H) and k_lat.shape[3] == hd,
+          "k_lat/v_lat must be (B, H, Lk, hd)")
+    Lk = k_lat.shape[2]
+    S, ctx_bs = 0, 0
+    if k_ctx is not None:
+        _cuda_contig("k_ctx", k_ctx)
+        _cuda_contig("v_ctx", v_ctx)
+        _need(k_ctx.shape == v_ctx.shape, "k_ctx and v_ctx differ in shape")
+        if k_ctx.dim() == 3:
+            S = k_ctx.shape[0]
+            _need(k_ctx.shape[1:] == (H, hd), "k_ctx must be (S, H, hd) or (B, S, H, hd)")
+        else:
+            _need(k_ctx.dim() == 4 and k_ctx.shape[0] == B and k_ctx.shape[2:] == (H, hd),
+                  "k_ctx must be (S, H, hd) or (B, S, H, hd)")
+            S, ctx_bs = k_ctx.shape[1], k_ctx.stride(0)
+    K = Lk + S
+    bias_bs = 0
+    if bias is not None:
+        _cuda_contig("bias", bias)
+        _need(bias.dtype == dt, "bias must have q's dtype")
+        _need(bias.numel() in (K, B * K), f"bias must hold K={K} or B*K values")
+        bias_bs = K if bias.numel() == B * K else 0
+    for t in (k_lat, v_lat, k_ctx, v_ctx):
+        _need(t is None or t.dtype == dt, "q, k, v must share one dtype")
+    if out is None:
+        out = torch.empty((B, L, H, hd), device=q.device, dtype=dt)
+    _cuda_contig("out", out)
+    _need(out.shape == (B, L, H, hd) and out.dtype == dt, "out must be (B, L, H, hd) in q's dtype")
+    check(lib().sk_dit_attention(_ptr(q), _ptr(k_lat), _ptr(v_lat), _ptr(k_ctx), _ptr(v_ctx), _ptr(bias), _ptr(out),
+                                 B, H, L, Lk, S, hd, ctx_bs, bias_bs, _dtype_code(dt), float(scale or 0.0), _stream()),
+          "sk_dit_attention")
+    return out
+
+
+def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, attn_mask: torch.Tensor | None = None) -> torch.Tensor:
+    """Drop-in for `F.scaled_dot_product_attention(q, k, v, attn_mask=bias)` at engine/fused.py:295.
+
+    q (B, H, L, hd), k/v (B, H, K, hd), attn_mask additive (B or 1, 1, 1, K) or bool (True = keep).
+    Returns (B, H, L, hd) whose memory is (B, L, H, hd)-contiguous, so `y.transpose(1, 2)` is
+    contiguous as the `gate` kernel reads it (engine/fused.py:296-298).
+    """
+    bias = None
+    if attn_mask is not None:
+        if attn_mask.dtype == torch.bool:
+            bias = torch.zeros(attn_mask.shape, device=q.device, dtype=q.dtype).masked_fill_(~attn_mask, float("-inf"))
+        else:
+            bias = attn_mask
+        bias = bias.reshape(-1, k.shape[2]).contiguous()
+    y = dit_attention(q, k, v, None, None, bias)
+    return y.transpose(1, 2)
+
+
+# ---- Qwen3 decode --------------------------------------------------------------------------------
+
+def decode_workspace_bytes(max_len: int, nq: int, nkv: int, hd: int = 128, cache_dtype: torch.dtype = torch.bfloat16) -> int:
+    return int(lib().sk_decode_workspace_bytes(max_len, nq, nkv, hd, _dtype_code(cache_dtype)))
+
+
+def decode_workspace(max_len: int, nq: int, nkv: int, device, hd: int = 128,
+                     cache_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """A zero-filled workspace for decode_attention (allocate before graph capture)."""
+    n = decode_workspace_bytes(max_len, nq, nkv, hd, cache_dtype)
+    return torch.zeros(max(n, 16), dtype=torch.uint8, device=device)
+
+
+def decode_attention(qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps: float, rope: torch.Tensor,
+                     Kc: torch.Tensor, Vc: torch.Tensor, pos_ptr: torch.Tensor | None, pos_add: int, max_len: int,
+                     nq: int, nkv: int, out: torch.Tensor, workspace: torch.Tensor | None) -> torch.Tensor:
+    """One talker layer's decode attention with the reference kernel's arguments
+    (qwen3/kernels.py:341-344): writes K/V at pos = pos_ptr[0] + pos_add and out (nq*128 fp32)."""
+    hd = Kc.shape[-1]
+    for n, t in (("qkv", qkv), ("qn", qn), ("kn", kn), ("rope", rope), ("Kc", Kc), ("Vc", Vc), ("out", out)):
+        _cuda_contig(n, t)
+    _need(qkv.dtype == torch.float32 and qkv.numel() == (nq + 2 * nkv) * hd, "qkv must be float32 [(nq+2nkv)*hd]")
+    _need(out.dtype == torch.float32 and out.numel() == nq * hd, "out must be float32 [nq*hd]")
+    _need(rope.dtype == torch.float32 and rope.numel() >= max_len * hd, "rope must be float32 [max_len][hd]")
+    _need(Kc.shape == Vc.shape and Kc.numel() == nkv * max_len * hd and Kc.dtype == Vc.dtype,
+          "Kc/Vc must be [nkv][max_len][hd]")
+    if pos_ptr is not None:
+        _need(pos_ptr.is_cuda and pos_ptr.dtype == torch.int64, "pos_ptr must be a CUDA int64 tensor")
+    ws_n = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().sk_decode_attention(_ptr(qkv), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
+                                    _ptr(pos_ptr), int(pos_add), int(max_len), int(nq), int(nkv), int(hd), _ptr(out),
+                                    _ptr(workspace), ws_n, _dtype_code(Kc.dtype), _stream()), "sk_decode_attention")
+    return out
+
+
+def version() -> int:
+    return int(lib().sk_version())
+
+
+__all__ = ["dit_qkv_prologue", "dit_attention", "sdpa", "decode_attention", "decode_workspace",
+           "decode_workspace_bytes", "device_error", "version", "_lib"]

@@ -1,0 +1,242 @@
+"""Request-parallel serving across GPUs, with no collectives.
+
+The reference serves one request at a time per process, one GPU per process
+(scripts/run_in_image.sh:24-33, README.md:186). Batch-1 TTS attention does not shard, so scaling
+to 1/2/4/8 B200 means independent requests pinned to GPUs:
+
+  * `plan_lpt`     longest-first greedy assignment of requests to workers (static, deterministic:
+                   every rank computes the same plan, nothing is exchanged);
+  * `run_sharded`  one rank's share, for a torchrun launch (used by bench.py);
+  * `serve_local`  a host-side queue feeding one worker process per GPU (CUDA_VISIBLE_DEVICES
+                   pinning); workers pull requests, and the requests of a worker that dies are
+                   put back on the queue for the survivors;
+  * `GpuExecutor`  runs one request's attention workload on a GPU: a DiT request is every
+                   attention call of one c2-shaped synthesis (24 layers x 20 steps, CFG on the
+                   first 10) at its latent length; a decode request is every talker-layer decode
+                   attention of one c3-shaped decode from the 96-token prompt to its final length.
+"""
+
+from __future__ import annotations
+
+import multiprocessing as mp
+import os
+import queue
+import time
+from dataclasses import dataclass
+
+
+@dataclass(frozen=True)
+class Request:
+    rid: int
+    kind: str      # "dit" or "decode"
+    size: int      # latent length L (dit) or final KV length T (decode)
+
+
+def requests_c4(seed: int = 0) -> list[Request]:
+    from .workloads import serving_requests
+    return [Request(i, k, s) for i, (k, s) in enumerate(serving_requests(seed))]
+
+
+def cost_estimate(r: Request) -> float:
+    """Rough device seconds: per call, the work at B200 rates plus a launch floor."""
+    if r.kind == "dit":
+        K = r.size + 512
+        calls = [3] * 240 + [1] * 240
+        return sum(4 * B * 16 * r.size * K * 128 / 5e14 + 5e-6 for B in calls)
+    steps = max(r.size - 96, 0)
+    return sum(28 * (2 * 8 * (96 + i) * 128 * 2 / 1.5e12 + 3e-6) for i in range(1, steps + 1))
+
+
+def plan_lpt(reqs: list[Request], n: int) -> list[list[Request]]:
+    """Longest processing time first: each request, largest first, goes to the least-loaded worker
+    (ties to the lowest index). Deterministic."""
+    loads = [0.0] * n
+    plan: list[list[Request]] = [[] for _ in range(n)]
+    for r in sorted(reqs, key=lambda r: (-cost_estimate(r), r.rid)):
+        i = min(range(n), key=lambda j: (loads[j], j))
+        plan[i].append(r)
+        loads[i] += cost_estimate(r)
+    return plan
+
+
+def run_sharded(reqs: list[Request], executor, rank: int, world: int) -> list[tuple[int, float]]:
+    """This rank's share of the plan; returns (rid, seconds) per request run."""
+    out = []
+    for r in plan_lpt(reqs, world)[rank]:
+        t0 = time.perf_counter()
+        executor.run(r)
+        out.append((r.rid, time.perf_counter() - t0))
+    return out
+
+
+# ---- host queue with worker processes ---------------------------------------------------------------
+
+def _worker(wid: int, device_env: str | None, make_executor, tasks, results):
+    if device_env is not None:
+        os.environ["CUDA_VISIBLE_DEVICES"] = device_env
+    ex = make_executor(wid)
+    while True:
+        r = tasks.get()
+        if r is None:
+            results.put(("exit", wid, None, 0.0))
+            return
+        results.put(("claim", wid, r.rid, 0.0))
+        t0 = time.perf_counter()
+        ex.run(r)
+        results.put(("done", wid, r.rid, time.perf_counter() - t0))
+
+
+def serve_local(reqs: list[Request], n_workers: int, make_executor, devices: list[str] | None = None,
+                timeout_s: float = 600.0) -> dict:
+    """Run every request once on `n_workers` spawned worker processes fed from one host queue.
+
+    make_executor(worker_id) builds the worker's executor inside the worker (picklable callable).
+    devices[i] is written to CUDA_VISIBLE_DEVICES of worker i. A worker that dies has its claimed,
+    unfinished requests re-queued. Returns {"done": {rid: (worker, seconds)}, "requeued": [...],
+    "dead": [...], "wall_s": ...}.
+    """
+    ctx = mp.get_context("spawn")
+    tasks, results = ctx.Queue(), ctx.Queue()
+    by_id = {r.rid: r for r in reqs}
+    for r in sorted(reqs, key=lambda r: (-cost_estimate(r), r.rid)):
+        tasks.put(r)
+    procs = {}
+    for w in range(n_workers):
+        env = devices[w] if devices else None
+        p = ctx.Process(target=_worker, args=(w, env, make_executor, tasks, results), daemon=True)
+        p.start()
+        procs[w] = p
+    claimed: dict[int, set[int]] = {w: set() for w in procs}
+    done: dict[int, tuple[int, float]] = {}
+    requeued, dead = [], []
+    t0 = time.perf_counter()
+    alive = set(procs)
+    sent_stop = False
+    while alive:
+        if time.perf_counter() - t0 > timeout_s:
+            for w in alive:
+                procs[w].kill()
+            raise TimeoutError("serving did not finish")
+        try:
+            kind, w, rid, sec = results.get(timeout=0.2)
+            if kind == "claim":
+                claimed[w].add(rid)
+            elif kind == "done":
+                claimed[w].discard(rid)
+                done[rid] = (w, sec)
+            elif kind == "exit":
+                alive.discard(w)
+        except queue.Empty:
+            pass
+        for w in list(alive):
+            if not procs[w].is_alive() and procs[w].exitcode not in (None, 0):
+                alive.discard(w)
+                dead.append(w)
+                for rid in sorted(claimed[w]):
+                    if rid not in done:
+                        requeued.append(rid)
+                        tasks.put(by_id[rid])
+                claimed[w].clear()
+        if len(done) == len(reqs) and not sent_stop:
+            for _ in range(n_workers):
+                tasks.put(None)
+            sent_stop = True
+        if not alive and len(done) < len(reqs):
+            raise RuntimeError(f"all workers died with {len(reqs) - len(done)} requests left")
+    for p in procs.values():
+        p.join(timeout=5)
+    return {"done": done, "requeued": requeued, "dead": dead, "wall_s": time.perf_counter() - t0}
+
+
+# ---- GPU executor --------------------------------------------------------------------------------------
+
+class GpuExecutor:
+    """Runs a request's attention workload on one GPU from CUDA graphs captured in `warm`."""
+
+    def __init__(self, device, max_cache: int = 1536):
+        import torch
+        self.torch = torch
+        self.device = torch.device(device)
+        self.max_cache = max_cache
+        self.dit = {}       # L -> (graph, buffers)
+        self.dec = None     # (graph, TalkerAttention, buffers)
+
+    def _dit_graph(self, L: int):
+        import torch
+
+        from . import dit, ops, workloads as W
+        sh = W.c4_dit(L)
+        g = torch.Generator(device=self.device).manual_seed(L)
+        bufs = {}
+        for B in (3, 1):
+            o4 = (torch.randn(B * L, 4 * sh.H * sh.hd, device=self.device, generator=g) * sh.sigma).bfloat16()
+            q, k, v = ops.dit_qkv_prologue(o4, W.dit_qk_weights(sh, self.device), W.dit_freqs(L, sh.hd, device=self.device),
+                                           B, L, sh.H, sh.hd, 1e-6)
+            bufs[B] = (q, k, v, torch.empty((B, L, sh.H, sh.hd), device=self.device, dtype=torch.bfloat16))
+        ctx = []
+        for _ in range(sh.n_layers):
+            kc = torch.randn(sh.S, sh.H, sh.hd, device=self.device, generator=g)
+            kc = (kc * torch.rsqrt(kc.pow(2).mean(-1, keepdim=True))).bfloat16()
+            vc = (torch.randn(sh.S, sh.H, sh.hd, device=self.device, generator=g) * sh.sigma).bfloat16()
+            ctx.append((kc, vc))
+        bias = dit.cfg_bias(L, sh.Tb, sh.Sp, L, 64, device=self.device)
+
+        def run():
+            for i, B in enumerate(sh.synthesis_calls()):
+                q, k, v, y = bufs[B]
+                kc, vc = ctx[i % sh.n_layers]
+                ops.dit_attention(q, k, v, kc, vc, bias[:B], out=y)
+
+        return self._capture(run), (bufs, ctx, bias)
+
+    def _decode_graph(self):
+        import torch
+
+        from . import qwen3, workloads as W
+        s = W.C3
+        ta = qwen3.TalkerAttention(s.n_layers, s.nq, s.nkv, self.max_cache, s.theta, s.eps, self.device, torch.bfloat16)
+        g = torch.Generator(device=self.device).manual_seed(3)
+        ta.k.copy_(torch.randn(ta.k.shape, device=self.device, generator=g))
+        ta.v.copy_(torch.randn(ta.v.shape, device=self.device, generator=g))
+        qkv = torch.randn(s.n_layers, (s.nq + 2 * s.nkv) * s.hd, device=self.device, generator=g)
+        qn = 1 + 0.02 * torch.randn(s.n_layers, s.hd, device=self.device, generator=g)
+        kn = 1 + 0.02 * torch.randn(s.n_layers, s.hd, device=self.device, generator=g)
+        out = torch.empty(s.n_layers, s.nq * s.hd, device=self.device)
+
+        def run():
+            for li in range(s.n_layers):
+                ta.attn(li, qkv[li], qn[li], kn[li], out[li])
+            ta.pos.add_(1)
+
+        ta.pos.fill_(s.prompt)
+        gr = self._capture(run)
+        return gr, ta, (qkv, qn, kn, out)
+
+    def _capture(self, fn):
+        torch = self.torch
+        st = torch.cuda.Stream(self.device)
+        st.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(st):
+            fn()
+        torch.cuda.current_stream(self.device).wait_stream(st)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        return gr
+
+    def warm(self, reqs: list[Request]):
+        for r in reqs:
+            if r.kind == "dit" and r.size not in self.dit:
+                self.dit[r.size] = self._dit_graph(r.size)
+            elif r.kind == "decode" and self.dec is None:
+                self.dec = self._decode_graph()
+
+    def run(self, r: Request):
+        self.warm([r])
+        if r.kind == "dit":
+            self.dit[r.size][0].replay()
+        else:
+            gr, ta, _ = self.dec
+            ta.pos.fill_(96)
+            for _ in range(96, min(r.size, self.max_cache)):
+                gr.replay()

@@ -1,0 +1,62 @@
+"""Host-side logic that needs no GPU: CFG bias construction, workload accounting, determinism."""
+
+import numpy as np
+import torch
+
+from conftest import load_golden
+from oracle import dit_attn_ref as D
+from sokutou_b200 import dit, qwen3, workloads as W
+
+
+def test_cfg_bias_matches_reference_masks():
+    z = load_golden("dit_masks")
+    for i in range(4):
+        p = f"case{i}_"
+        args = [int(z[p + k]) for k in ("lb", "tb", "n_spk", "seq_len", "n_text")]
+        assert np.array_equal(dit.cfg_key_mask(*args).numpy(), z[p + "mask3"])
+        b = dit.cfg_bias(*args, dtype=torch.float32).numpy()
+        assert np.array_equal(b, z[p + "bias3"])
+
+
+def test_flop_and_byte_accounting():
+    assert W.C0.flops(3) == 1_207_959_552
+    assert W.C2.flops(3) == 12_884_901_888
+    # per synthesis, 10 steps B=3 + 10 steps B=1
+    assert abs(W.c1(128).synthesis_flops() - 7.248e10) / 7.248e10 < 1e-3
+    assert abs(W.c1(256).synthesis_flops() - 1.933e11) / 1.933e11 < 1e-3
+    assert abs(W.c1(512).synthesis_flops() - 5.798e11) / 5.798e11 < 1e-3
+    assert abs(W.C2.synthesis_flops() - 4.123e12) / 4.123e12 < 1e-3
+    assert W.C3.layer_bytes(1120) == 4_616_192
+    assert W.C3.decode_bytes() == 72_284_635_136
+    assert len(W.c1(256).synthesis_calls()) == 240
+
+
+def test_workload_inputs_are_seeded():
+    a = W.dit_call_inputs(W.C0, 3, seed=0)
+    b = W.dit_call_inputs(W.C0, 3, seed=0)
+    c = W.dit_call_inputs(W.C0, 3, seed=1)
+    assert torch.equal(a["o4"], b["o4"]) and not torch.equal(a["o4"], c["o4"])
+    assert 16 <= a["n_text"] <= 64
+    assert a["o4"].shape == (3 * 256, 4 * 12 * 64)
+    assert a["bias3"].shape == (3, 512)
+    # ctx keys arrive unit-RMS per head
+    rms = a["ctx_k"].pow(2).mean(-1).sqrt()
+    assert torch.allclose(rms, torch.ones_like(rms), atol=1e-3)
+
+
+def test_freqs_table_matches_oracle():
+    assert np.allclose(W.dit_freqs(300, 64).numpy(), D.rope_freqs(300, 64), atol=1e-6)
+
+
+def test_qwen3_rope_table_matches_oracle():
+    from oracle import decode_attn_ref as Q
+    assert np.allclose(qwen3.rope_table(1200, 1e6).numpy(), Q.rope_table(1200), atol=2e-6)
+
+
+def test_serving_requests_seeded():
+    r = W.serving_requests(0)
+    assert len(r) == 64
+    assert sum(k == "dit" for k, _ in r) == 32
+    assert all(96 <= s <= 384 for k, s in r if k == "dit")
+    assert all(200 <= s <= 1500 for k, s in r if k == "decode")
+    assert r == W.serving_requests(0)
