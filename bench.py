@@ -422,6 +422,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-serving", action="store_true")
+    ap.add_argument("--only-c1", action="store_true", help="headline workload only (for launch-list captures)")
     a = ap.parse_args()
     if a.impl == "reference":
         return reference_arm(a)
@@ -453,6 +454,12 @@ def main():
         t = time_graphs([s.graph], a.steps, 1, dist) / a.steps
         per_L[f"L{s.shape.L}"] = {"tflops": round(s.flops / (t / 1e3) / 1e12, 2), "ms_per_synthesis": round(t, 4),
                                   "us_per_call": round(t * 1e3 / len(s.calls), 3)}
+    if a.only_c1:
+        if dist.rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(value, 3), "unit": UNIT, "ms_per_step": round(ms_step, 4),
+                              "per_L": per_L, "note": "--only-c1: headline timing only"}), flush=True)
+        dist.close()
+        return
     e2e_ms, h2d, d2h = dit_e2e(syn, max(1, a.steps // 5), 1, dist, dev)
     e2e_steps = max(1, a.steps // 5)
     e2e_val = dist.sum(flops_step) / (e2e_ms / e2e_steps / 1e3) / 1e12

@@ -20,6 +20,7 @@ constexpr int kHD = 128;     // head dim (reference: HD 128, qwen3/kernels.py:38
 constexpr int kG = 2;        // q heads per kv head (reference: nq == 2*nkv, qwen3/kernels.py:457)
 constexpr int kChunk = 64;   // keys per CTA
 constexpr int kThreads = 128;
+constexpr int kMaxSplits = 256;  // max_len <= 16384
 
 template <typename CT>
 struct Cache;
@@ -88,6 +89,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(
   __shared__ float red[8][4];
   __shared__ float stat[kG][2];
   __shared__ int is_last;
+  __shared__ float mg_s[kMaxSplits * kG];  // merge: chunk maxima, then chunk weights
+  __shared__ float lg_s[kMaxSplits * kG];  // merge: chunk sums
   __shared__ __align__(8) uint64_t bar;
 
   const int kvh = blockIdx.y, split = blockIdx.x;
@@ -310,19 +313,50 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  // thread t merges dimension d = t of both heads
-#pragma unroll
-  for (int g = 0; g < kG; ++g) {
+  // Merge. Every load below is issued independently of the others (no dependent chain through
+  // L2): the per-chunk (max, sum) pairs are staged in shared memory by one thread each, then each
+  // thread combines its dimension over the chunks, 8 chunks' partials in flight at a time.
+  for (int i = t; i < active * kG; i += kThreads) {
+    const size_t sl = (size_t)kvh * nsplit + i / kG;
+    mg_s[i] = __ldcg(ws.ml + (sl * kG + (i % kG)) * 2);
+    lg_s[i] = __ldcg(ws.ml + (sl * kG + (i % kG)) * 2 + 1);
+  }
+  __syncthreads();
+  if (w < kG) {  // warp g: global max and denominator of head g, weights per chunk
+    const int g = w;
     float M = -INFINITY;
-    for (int sp = 0; sp < active; ++sp) M = fmaxf(M, __ldcg(ws.ml + (((size_t)kvh * nsplit + sp) * kG + g) * 2));
-    float num = 0.f, den = 0.f;
-    for (int sp = 0; sp < active; ++sp) {
-      const size_t sl = (size_t)kvh * nsplit + sp;
-      const float f = expf(__ldcg(ws.ml + (sl * kG + g) * 2) - M);
-      num += f * __ldcg(ws.o + (sl * kG + g) * kHD + d);
-      den += f * __ldcg(ws.ml + (sl * kG + g) * 2 + 1);
+    for (int sp = lane; sp < active; sp += 32) M = fmaxf(M, mg_s[sp * kG + g]);
+    M = warp_max(M);
+    float den = 0.f;
+    for (int sp = lane; sp < active; sp += 32) {
+      const float f = expf(mg_s[sp * kG + g] - M);
+      mg_s[sp * kG + g] = f;  // now the chunk weight
+      den += f * lg_s[sp * kG + g];
     }
-    out[(size_t)(kvh * kG + g) * kHD + d] = num / den;
+    den = warp_sum(den);
+    if (lane == 0) stat[g][1] = den;
+  }
+  __syncthreads();
+  {
+    float num[kG] = {};
+    const float* ob = ws.o + (size_t)kvh * nsplit * kG * kHD + d;
+    int sp = 0;
+    for (; sp + 8 <= active; sp += 8) {
+      float v[8][kG];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int g = 0; g < kG; ++g) v[u][g] = __ldcg(ob + ((size_t)(sp + u) * kG + g) * kHD);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int g = 0; g < kG; ++g) num[g] += mg_s[(sp + u) * kG + g] * v[u][g];
+    }
+    for (; sp < active; ++sp)
+#pragma unroll
+      for (int g = 0; g < kG; ++g) num[g] += mg_s[sp * kG + g] * __ldcg(ob + ((size_t)sp * kG + g) * kHD);
+#pragma unroll
+    for (int g = 0; g < kG; ++g) out[(size_t)(kvh * kG + g) * kHD + d] = num[g] / stat[g][1];
   }
   if (t == 0) ws.cnt[kvh] = 0;  // ready for the next call (and graph replay)
 }
@@ -351,6 +385,7 @@ extern "C" int sk_decode_attention(const float* qkv, const float* qn, const floa
   if ((reinterpret_cast<uintptr_t>(Kc) | reinterpret_cast<uintptr_t>(Vc) | reinterpret_cast<uintptr_t>(out)) & 15)
     return SK_ERR_INVALID_ARG;
   const int nsplit = (max_len + decode::kChunk - 1) / decode::kChunk;
+  if (nsplit > decode::kMaxSplits) return SK_ERR_UNSUPPORTED;
   if (nsplit > 1 && (!workspace || ws_bytes < decode::ws_bytes(max_len, nkv))) return SK_ERR_WORKSPACE;
   if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 15)) return SK_ERR_INVALID_ARG;
   int rc = sk_check_device();

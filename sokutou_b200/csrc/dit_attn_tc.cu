@@ -3,17 +3,23 @@
 // Replaces F.scaled_dot_product_attention(q, k, v, attn_mask=bias) at engine/fused.py:295.
 // One CTA computes a 128-row query tile of one (batch, head) against all K = Lk + S keys:
 //
-//   warp 4 (one lane)  TMA producer: Q once, then K/V tiles of 128 keys into a 2-stage ring.
+//   warp 4 (one lane)  TMA producer: Q once, then K and V tiles of 128 keys into two rings of
+//                      NSK and NSV slots. The rings are released independently: a K slot frees as
+//                      soon as S = Q·Kᵀ has consumed it, a V slot when O += P·V has. The producer
+//                      polls both rings, so neither blocks the other.
 //                      Latent keys come from (B, H, Lk, hd); conditioning keys straight from their
 //                      batch-shared (S, H, hd) buffer — no per-CFG-branch copy.
 //   warp 5 (one lane)  MMA issuer: S_j = Q·K_jᵀ into one of two TMEM S buffers (128 fp32 columns
-//                      each), then O += P_j·V_j into the TMEM O accumulator (hd columns).
+//                      each), issued one tile ahead, then O += P_j·V_j into the TMEM O accumulator.
 //   warps 0-3          softmax: thread t owns query row t = TMEM lane t. It loads its S row
-//                      (tcgen05.ld), adds the key bias, keeps a running max in the log2 domain,
-//                      writes P_j (bf16) into a 128B-swizzled shared-memory tile for the next MMA,
-//                      and rescales O in TMEM only when its max grew by more than 2^8 (the result
-//                      is exact either way: numerator and denominator share the stale max).
-//                      Epilogue: O / l → bf16 → y (B, L, H, hd).
+//                      (tcgen05.ld), applies scale and key bias with packed fp32x2 FMAs, keeps a
+//                      running max in the log2 domain, writes P_j (bf16) into a 128B-swizzled
+//                      shared-memory tile, and rescales O in TMEM only when its max grew by more
+//                      than 2^8 (exact either way: numerator and denominator share the stale max).
+//                      Epilogue: O / l -> bf16 -> y (B, L, H, hd).
+// Every thread executes griddepcontrol.wait before touching global memory, so with programmatic
+// dependent launch a kernel's set-up (barriers, TMEM, descriptor prefetch) overlaps the tail of
+// the kernel before it while every input read still follows that kernel's completion.
 //
 // Operand layouts (all 128-byte swizzled, 1024-byte aligned, as TMA writes them):
 //   Q [128 rows][hd]   K-major A of S = Q·Kᵀ      (hd split in 64-element chunks)
@@ -28,25 +34,37 @@
 namespace sk {
 namespace dit {
 
-constexpr int kBM = 128, kBN = 128, kNST = 2, kNP = 2;
+constexpr int kBM = 128, kBN = 128;
 constexpr int kThreadsTC = 192;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
 
 template <int HD>
+struct TcCfg;
+template <>
+struct TcCfg<64> {  // 16 + 4*16 + 4*16 + 2*32 = 208 KB
+  static constexpr int NSK = 4, NSV = 4, NP = 2;
+};
+template <>
+struct TcCfg<128> {  // 32 + 3*32 + 2*32 + 1*32 = 224 KB
+  static constexpr int NSK = 3, NSV = 2, NP = 1;
+};
+
+template <int HD>
 struct TcLayout {
+  static constexpr int NSK = TcCfg<HD>::NSK, NSV = TcCfg<HD>::NSV, NP = TcCfg<HD>::NP;
   static constexpr int NCH = HD / 64;              // 64-element (128-byte) chunks per row
   static constexpr int Q_BYTES = kBM * HD * 2;
   static constexpr int KV_BYTES = kBN * HD * 2;
   static constexpr int P_BYTES = kBM * kBN * 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + kNST * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + kNST * KV_BYTES;
-  static constexpr int OFF_BIAS = OFF_P + kNP * P_BYTES;  // float [2][kBN]
+  static constexpr int OFF_V = OFF_K + NSK * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + NSV * KV_BYTES;
+  static constexpr int OFF_BIAS = OFF_P + NP * P_BYTES;  // float [2][kBN]
   static constexpr int OFF_BAR = OFF_BIAS + 2 * kBN * 4;
-  // barriers: q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2], o_done[2], mma_done
-  static constexpr int NBAR = 1 + 3 * kNST + 2 + 2 + 2 * kNP + 1;
+  // q_full, k_full/k_empty[NSK], v_full/v_empty[NSV], s_full[2], s_free[2], p_full[NP], o_done[NP], mma_done
+  static constexpr int NBAR = 1 + 2 * NSK + 2 * NSV + 4 + 2 * NP + 1;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
   static constexpr int SMEM_ALLOC = BYTES + 1024;  // slack to align the base to 1024
@@ -63,12 +81,22 @@ struct TcParams {
   int* err;
 };
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 template <int HD>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
                    const __grid_constant__ CUtensorMap tmVc, const TcParams prm) {
   using Ly = TcLayout<HD>;
+  constexpr int NSK = Ly::NSK, NSV = Ly::NSV, NP = Ly::NP;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -76,13 +104,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly::OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + kNST;
-  uint64_t* kv_empty = v_full + kNST;
-  uint64_t* s_full = kv_empty + kNST;
+  uint64_t* k_empty = k_full + NSK;
+  uint64_t* v_full = k_empty + NSK;
+  uint64_t* v_empty = v_full + NSV;
+  uint64_t* s_full = v_empty + NSV;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
-  uint64_t* o_done = p_full + kNP;
-  uint64_t* mma_done = o_done + kNP;
+  uint64_t* o_done = p_full + NP;
+  uint64_t* mma_done = o_done + NP;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::OFF_TMEM);
   float* bias_s = reinterpret_cast<float*>(smem + Ly::OFF_BIAS);
 
@@ -93,21 +122,33 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < kNST; ++i) {
+    for (int i = 0; i < NSK; ++i) {
       mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < NSV; ++i) {
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
     }
-    for (int i = 0; i < kNP; ++i) {
+    for (int i = 0; i < NP; ++i) {
       mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(mma_done, 1);
     fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    if (n_ctx) {
+      tma_prefetch_desc(&tmKc);
+      tma_prefetch_desc(&tmVc);
+    }
   }
   if (warp == 5) {
     tmem_alloc(tmem_slot, 512);
@@ -116,60 +157,68 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Inputs may come from the kernel launched before this one: wait for it, then let the next
+  // kernel start its own set-up.
+  griddep_wait();
+  griddep_launch_dependents();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS0 = tmem, tO = tmem + 256;
 
   if (warp == 4) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      if (n_ctx) {
-        tma_prefetch_desc(&tmKc);
-        tma_prefetch_desc(&tmVc);
-      }
       const int bh = b * prm.H + h;
+      const int bc = prm.ctx_batched ? b : 0;
       mbar_arrive_expect_tx(q_full, Ly::Q_BYTES);
 #pragma unroll
       for (int c = 0; c < Ly::NCH; ++c)
         tma_load_3d(smem + Ly::OFF_Q + c * (kBM * 128), &tmQ, q_full, c * 64, q0, bh);
-      int issued = 0;
+      // K_j and V_j are issued as soon as their ring slot is free, each ring on its own.
+      int jk = 0, jv = 0;
       bool ok = true;
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int s = j % kNST;
-        if (j >= kNST) ok = mbar_wait(&kv_empty[s], ((j / kNST) - 1) & 1, prm.err);
-        if (!ok) break;
-        uint8_t* kd = smem + Ly::OFF_K + s * Ly::KV_BYTES;
-        uint8_t* vd = smem + Ly::OFF_V + s * Ly::KV_BYTES;
-        mbar_arrive_expect_tx(&k_full[s], Ly::KV_BYTES);
-        if (j < n_lat) {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ok && (jk < ntiles || jv < ntiles)) {
+        bool progress = false;
+        if (jk < ntiles && (jk < NSK || mbar_try_wait(&k_empty[jk % NSK], ((jk / NSK) - 1) & 1))) {
+          const int s = jk % NSK;
+          uint8_t* dst = smem + Ly::OFF_K + s * Ly::KV_BYTES;
+          mbar_arrive_expect_tx(&k_full[s], Ly::KV_BYTES);
+          if (jk < n_lat) {
 #pragma unroll
-          for (int c = 0; c < Ly::NCH; ++c) tma_load_3d(kd + c * (kBN * 128), &tmK, &k_full[s], c * 64, j * kBN, bh);
-        } else {
-          const int jc = j - n_lat, bc = prm.ctx_batched ? b : 0;
+            for (int c = 0; c < Ly::NCH; ++c) tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, jk * kBN, bh);
+          } else {
 #pragma unroll
-          for (int c = 0; c < Ly::NCH; ++c)
-            tma_load_4d(kd + c * (kBN * 128), &tmKc, &k_full[s], c * 64, h, jc * kBN, bc);
+            for (int c = 0; c < Ly::NCH; ++c)
+              tma_load_4d(dst + c * (kBN * 128), &tmKc, &k_full[s], c * 64, h, (jk - n_lat) * kBN, bc);
+          }
+          ++jk;
+          progress = true;
         }
-        mbar_arrive_expect_tx(&v_full[s], Ly::KV_BYTES);
-        if (j < n_lat) {
+        if (jv < ntiles && jv < jk && (jv < NSV || mbar_try_wait(&v_empty[jv % NSV], ((jv / NSV) - 1) & 1))) {
+          const int s = jv % NSV;
+          uint8_t* dst = smem + Ly::OFF_V + s * Ly::KV_BYTES;
+          mbar_arrive_expect_tx(&v_full[s], Ly::KV_BYTES);
+          if (jv < n_lat) {
 #pragma unroll
-          for (int c = 0; c < Ly::NCH; ++c) tma_load_3d(vd + c * (kBN * 128), &tmV, &v_full[s], c * 64, j * kBN, bh);
-        } else {
-          const int jc = j - n_lat, bc = prm.ctx_batched ? b : 0;
+            for (int c = 0; c < Ly::NCH; ++c) tma_load_3d(dst + c * (kBN * 128), &tmV, &v_full[s], c * 64, jv * kBN, bh);
+          } else {
 #pragma unroll
-          for (int c = 0; c < Ly::NCH; ++c)
-            tma_load_4d(vd + c * (kBN * 128), &tmVc, &v_full[s], c * 64, h, jc * kBN, bc);
+            for (int c = 0; c < Ly::NCH; ++c)
+              tma_load_4d(dst + c * (kBN * 128), &tmVc, &v_full[s], c * 64, h, (jv - n_lat) * kBN, bc);
+          }
+          ++jv;
+          progress = true;
         }
-        issued = j + 1;
+        if (!progress && (++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
+          ok = false;
+        }
       }
       // Keep shared memory alive until every copy issued has landed (already true on the normal path).
       mbar_wait(q_full, 0, prm.err);
-      for (int j = (issued > kNST ? issued - kNST : 0); j < issued; ++j) {
-        mbar_wait(&k_full[j % kNST], (j / kNST) & 1, prm.err);
-        mbar_wait(&v_full[j % kNST], (j / kNST) & 1, prm.err);
-      }
+      for (int j = (jk > NSK ? jk - NSK : 0); j < jk; ++j) mbar_wait(&k_full[j % NSK], (j / NSK) & 1, prm.err);
+      for (int j = (jv > NSV ? jv - NSV : 0); j < jv; ++j) mbar_wait(&v_full[j % NSV], (j / NSV) & 1, prm.err);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------------ MMA issuer
@@ -179,8 +228,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const uint32_t aQ = sbase + Ly::OFF_Q, aK = sbase + Ly::OFF_K, aV = sbase + Ly::OFF_V, aP = sbase + Ly::OFF_P;
       bool ok = mbar_wait(q_full, 0, prm.err);
       auto issue_s = [&](int j) -> bool {
-        const int s = j % kNST, sb = j & 1;
-        if (!mbar_wait(&k_full[s], (j / kNST) & 1, prm.err)) return false;
+        const int s = j % NSK, sb = j & 1;
+        if (!mbar_wait(&k_full[s], (j / NSK) & 1, prm.err)) return false;
         if (j >= 2 && !mbar_wait(&s_free[sb], ((j - 2) >> 1) & 1, prm.err)) return false;
         tc_fence_after();
 #pragma unroll
@@ -191,14 +240,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     smem_desc_sw128(aK + s * Ly::KV_BYTES + offk, 16, 1024), idS, kk > 0);
         }
         tc_commit(&s_full[sb]);
+        tc_commit(&k_empty[s]);  // the K slot is free once this S is computed
         return true;
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < ntiles && ok; ++j) {
         if (j + 1 < ntiles) ok = issue_s(j + 1);
         if (!ok) break;
-        const int s = j % kNST, pb = j & 1;
-        if (!mbar_wait(&p_full[pb], (j >> 1) & 1, prm.err) || !mbar_wait(&v_full[s], (j / kNST) & 1, prm.err)) {
+        const int sv = j % NSV, pb = j % NP;
+        if (!mbar_wait(&p_full[pb], (j / NP) & 1, prm.err) || !mbar_wait(&v_full[sv], (j / NSV) & 1, prm.err)) {
           ok = false;
           break;
         }
@@ -207,10 +257,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint32_t offp = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
           tc_mma_ss(tO, smem_desc_sw128(aP + pb * Ly::P_BYTES + offp, 16, 1024),
-                    smem_desc_sw128(aV + s * Ly::KV_BYTES + kk * 2048, kBN * 128, 1024), idO, (j > 0 || kk > 0));
+                    smem_desc_sw128(aV + sv * Ly::KV_BYTES + kk * 2048, kBN * 128, 1024), idO, (j > 0 || kk > 0));
         }
         tc_commit(&o_done[pb]);
-        tc_commit(&kv_empty[s]);
+        tc_commit(&v_empty[sv]);
       }
       tc_commit(mma_done);
       mbar_wait(mma_done, 0, prm.err);
@@ -221,6 +271,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(prm.bias);
     uint8_t* prow_base = smem + Ly::OFF_P + row * 128;
+    const float2 sl2 = make_float2(prm.scale_log2, prm.scale_log2);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
@@ -251,12 +302,19 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[sb]);
+      // t = s·scale·log2e + bias·log2e, packed two at a time; running row max with 3-input max
       float mt = -INFINITY;
-      const float* bt = bias_s + sb * kBN;
+      const float4* bt4 = reinterpret_cast<const float4*>(bias_s + sb * kBN);
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        x[c] = fmaf(x[c], prm.scale_log2, bt[c]);
-        mt = fmaxf(mt, x[c]);
+      for (int c = 0; c < kBN; c += 4) {
+        const float4 bb = bt4[c >> 2];
+        float2 t0 = __ffma2_rn(make_float2(x[c], x[c + 1]), sl2, make_float2(bb.x, bb.y));
+        float2 t1 = __ffma2_rn(make_float2(x[c + 2], x[c + 3]), sl2, make_float2(bb.z, bb.w));
+        x[c] = t0.x;
+        x[c + 1] = t0.y;
+        x[c + 2] = t1.x;
+        x[c + 3] = t1.y;
+        mt = max3(mt, max3(t0.x, t0.y, t1.x), t1.y);
       }
       const float m_new = fmaxf(m_run, mt);
       const bool want = m_new > m_run + kRescaleLog2;  // false while every key seen is masked
@@ -264,7 +322,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         // warp-uniform: every lane of the warp moves to its exact current max
         const float alpha = (m_new == -INFINITY) ? 1.f : ex2_approx(m_run - m_new);
         if (j > 0) {
-          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, prm.err)) {
+          if (!mbar_wait(&o_done[(j - 1) % NP], ((j - 1) / NP) & 1, prm.err)) {
             ok = false;
             break;
           }
@@ -284,22 +342,23 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         m_run = m_new;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      // P buffer sb was read by PV_{j-2}
-      if (j >= 2 && !mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, prm.err)) {
+      const float2 nm = make_float2(-m_use, -m_use);
+      // P buffer (j % NP) was last read by PV_{j-NP}
+      if (j >= NP && !mbar_wait(&o_done[j % NP], ((j / NP) - 1) & 1, prm.err)) {
         ok = false;
         break;
       }
-      float lsum = 0.f;
-      uint8_t* prow = prow_base + sb * Ly::P_BYTES;
+      float2 lsum = make_float2(0.f, 0.f);
+      uint8_t* prow = prow_base + (j % NP) * Ly::P_BYTES;
 #pragma unroll
       for (int u = 0; u < kBN / 8; ++u) {  // 16 units of 8 keys = 16 bytes
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(x[8 * u + 2 * e] - m_use);
-          const float p1 = ex2_approx(x[8 * u + 2 * e + 1] - m_use);
-          const __nv_bfloat162 pb2 = __floats2bfloat162_rn(p0, p1);
-          lsum += __low2float(pb2) + __high2float(pb2);
+          const float2 d = __fadd2_rn(make_float2(x[8 * u + 2 * e], x[8 * u + 2 * e + 1]), nm);
+          const float2 p = make_float2(ex2_approx(d.x), ex2_approx(d.y));
+          lsum = __fadd2_rn(lsum, p);
+          const __nv_bfloat162 pb2 = __floats2bfloat162_rn(p.x, p.y);
           pk[e] = *reinterpret_cast<const uint32_t*>(&pb2);
         }
         const int chunk = u >> 3, unit = u & 7;
@@ -308,13 +367,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                      "r"(pk[2]), "r"(pk[3])
                      : "memory");
       }
-      l_run += lsum;
+      l_run += lsum.x + lsum.y;
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full[sb]);
+      mbar_arrive(&p_full[j % NP]);
     }
     // ---- epilogue: y = O / l
-    if (ok && mbar_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, prm.err)) {
+    if (ok && mbar_wait(&o_done[(ntiles - 1) % NP], ((ntiles - 1) / NP) & 1, prm.err)) {
       tc_fence_after();
       const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
       const int qi = q0 + row;
@@ -417,8 +476,17 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
       return SK_ERR_CUDA;
     attr_done[dev] = true;
   }
-  dim3 grid((L + kBM - 1) / kBM, H, B), block(kThreadsTC);
-  attn_tc_kernel<HD><<<grid, block, smem, st>>>(mq, mk, mv, mkc, mvc, prm);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((L + kBM - 1) / kBM, H, B);
+  cfg.blockDim = dim3(kThreadsTC);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // set-up overlaps the previous kernel
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<HD>, mq, mk, mv, mkc, mvc, prm) != cudaSuccess) return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }
 

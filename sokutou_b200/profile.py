@@ -1,0 +1,103 @@
+"""Small, self-contained runs of one kernel for timing and for ncu captures.
+
+    python -m sokutou_b200.profile --case dit_c1_L512_b3 [--reps 50] [--graph]
+    python -m sokutou_b200.profile --case decode_T1120 [--reps 50] [--graph]
+
+Prints one JSON line: average microseconds per call from CUDA events over `reps` back-to-back calls
+(eager launches, or one CUDA graph holding them with --graph), and the algorithmic work per call.
+Inputs: distinct buffers per call, rotated over `--sets` copies so that a run can exceed L2.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import dit, ops, qwen3, workloads as W
+
+CASES = {
+    # name: (kind, shape args)
+    "dit_c1_L128_b3": ("dit", W.c1(128), 3), "dit_c1_L128_b1": ("dit", W.c1(128), 1),
+    "dit_c1_L256_b3": ("dit", W.c1(256), 3), "dit_c1_L256_b1": ("dit", W.c1(256), 1),
+    "dit_c1_L512_b3": ("dit", W.c1(512), 3), "dit_c1_L512_b1": ("dit", W.c1(512), 1),
+    "dit_c2_b3": ("dit", W.C2, 3), "dit_c2_b1": ("dit", W.C2, 1),
+    "decode_T128": ("decode", 128, None), "decode_T512": ("decode", 512, None),
+    "decode_T1120": ("decode", 1120, None), "decode_T1500": ("decode", 1500, None),
+}
+
+
+def dit_case(shape, B, sets, dev):
+    g = torch.Generator(device=dev).manual_seed(0)
+    H, hd, L, S = shape.H, shape.hd, shape.L, shape.S
+    calls = []
+    for _ in range(sets):
+        q, k, v = (torch.randn(B, H, L, hd, device=dev, generator=g).bfloat16() for _ in range(3))
+        kc = torch.randn(S, H, hd, device=dev, generator=g).bfloat16()
+        vc = torch.randn(S, H, hd, device=dev, generator=g).bfloat16()
+        y = torch.empty(B, L, H, hd, device=dev, dtype=torch.bfloat16)
+        calls.append((q, k, v, kc, vc, y))
+    bias = dit.cfg_bias(L, shape.Tb, shape.Sp, L, 40, device=dev)[:B].contiguous()
+    fns = [lambda c=c: ops.dit_attention(c[0], c[1], c[2], c[3], c[4], bias, out=c[5]) for c in calls]
+    return fns, shape.flops(B), "flop"
+
+
+def decode_case(T, sets, dev):
+    s = W.C3
+    max_len = 1536
+    g = torch.Generator(device=dev).manual_seed(0)
+    fns = []
+    for _ in range(sets):
+        ta = qwen3.TalkerAttention(1, s.nq, s.nkv, max_len, s.theta, s.eps, dev, torch.bfloat16)
+        ta.k.copy_(torch.randn(ta.k.shape, device=dev, generator=g))
+        ta.v.copy_(torch.randn(ta.v.shape, device=dev, generator=g))
+        ta.pos.fill_(T - 1)
+        qkv = torch.randn((s.nq + 2 * s.nkv) * s.hd, device=dev, generator=g)
+        qn = torch.ones(s.hd, device=dev)
+        out = torch.empty(s.nq * s.hd, device=dev)
+        fns.append(lambda ta=ta, qkv=qkv, qn=qn, out=out: ta.attn(0, qkv, qn, qn, out))
+    return fns, s.layer_bytes(T), "byte"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", required=True, choices=sorted(CASES))
+    ap.add_argument("--reps", type=int, default=50)
+    ap.add_argument("--sets", type=int, default=4)
+    ap.add_argument("--graph", action="store_true")
+    a = ap.parse_args()
+    dev = torch.device("cuda:0")
+    kind, x, B = CASES[a.case]
+    fns, work, unit = dit_case(x, B, a.sets, dev) if kind == "dit" else decode_case(x, a.sets, dev)
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    seq = [fns[i % len(fns)] for i in range(a.reps)]
+    run = lambda: [f() for f in seq]
+    if a.graph:
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            run()
+        torch.cuda.current_stream().wait_stream(st)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            run()
+        run = gr.replay
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    run()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / a.reps
+    rate = work / (us * 1e-6) / (1e12 if unit == "flop" else 1e9)
+    print(json.dumps({"case": a.case, "graph": a.graph, "reps": a.reps, "us_per_call": round(us, 3),
+                      f"{unit}s_per_call": work, ("TFLOP/s" if unit == "flop" else "GB/s"): round(rate, 2),
+                      "device_error": ops.device_error()}))
+
+
+if __name__ == "__main__":
+    main()
