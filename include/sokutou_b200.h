@@ -45,6 +45,7 @@ extern "C" {
 #define SK_ERR_CUDA (-3)          /* a CUDA runtime call failed (launch, attribute, ...) */
 #define SK_ERR_DEVICE (-4)        /* the current device is not an sm_100 part */
 #define SK_ERR_WORKSPACE (-5)     /* workspace missing or smaller than sk_decode_workspace_bytes() */
+#define SK_ERR_TOO_LARGE (-6)     /* the call needs more scratch than sk_decode_attention_noalloc holds */
 
 /* device error word values (sk_device_error) */
 #define SK_DEVERR_NONE 0
@@ -138,6 +139,27 @@ SK_API int sk_decode_attention(const float* qkv, const float* qn, const float* k
                         const float* rope, void* Kc, void* Vc,
                         const long long* pos_ptr, int pos_add, int max_len, int nq, int nkv, int hd,
                         float* out, void* workspace, size_t ws_bytes, int cache_dtype, void* stream);
+
+/*
+ * sk_decode_attention without a workspace argument: allocates nothing, for callers that cannot call
+ * cudaMalloc when they attend (a serving process that reserves its device memory up front and
+ * forbids allocation afterwards, a driver running inside a CUDA graph capture, a foreign-language
+ * binding that only passes buffers it already owns). No counterpart in the reference: its kernel
+ * (qwen3/kernels.py:338-414) keeps all scores in shared memory and needs no scratch.
+ *
+ * Same arguments and results as sk_decode_attention. The split-KV scratch is a 1 MiB array inside
+ * the library's device image, one per device that loads the library, kept until the process exits.
+ *   - Limit: the partials must fit 1 MiB minus 4 KiB, i.e. about nkv * ceil(max_len / 64) * 1040 bytes
+ *     (nkv = 8: max_len up to 7936); larger calls return SK_ERR_TOO_LARGE and launch nothing.
+ *   - The first call on each device looks up the array's address and zero-fills it, synchronously:
+ *     make that first call before any stream capture.
+ *   - Every call shares the array. Calls that may run at the same time on the GPU (different streams,
+ *     or graphs replayed concurrently) race on it; serialise them or use sk_decode_attention.
+ */
+SK_API int sk_decode_attention_noalloc(const float* qkv, const float* qn, const float* kn, float eps,
+                        const float* rope, void* Kc, void* Vc,
+                        const long long* pos_ptr, int pos_add, int max_len, int nq, int nkv, int hd,
+                        float* out, int cache_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libs
 
 SK_OK = 0
 ERRORS = {-1: "SK_ERR_INVALID_ARG", -2: "SK_ERR_UNSUPPORTED", -3: "SK_ERR_CUDA", -4: "SK_ERR_DEVICE",
-          -5: "SK_ERR_WORKSPACE"}
+          -5: "SK_ERR_WORKSPACE", -6: "SK_ERR_TOO_LARGE"}
 DEVICE_ERRORS = {0: "SK_DEVERR_NONE", 1: "SK_DEVERR_POS_RANGE", 2: "SK_DEVERR_TIMEOUT"}
 SK_BF16, SK_F32 = 0, 1
 
@@ -27,6 +27,7 @@ SIGNATURES = {
     "sk_dit_qkv_prologue": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
     "sk_decode_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "sk_decode_attention": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
+    "sk_decode_attention_noalloc": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P]),
 }
 
 _lib = None

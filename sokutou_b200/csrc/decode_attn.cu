@@ -11,6 +11,8 @@
 //   chunk-local softmax (expf like the reference) and PV; the last CTA of a KV head to finish
 //   merges the per-chunk (max, sum, o) partials — an atomic counter, no spin-wait.
 // The position comes from device memory (pos_ptr[0] + pos_add) so one CUDA graph serves all steps.
+#include <mutex>
+
 #include "sk_common.cuh"
 
 namespace sk {
@@ -415,4 +417,63 @@ extern "C" int sk_decode_attention(const float* qkv, const float* qn, const floa
                                                                   max_len, nq, nkv, out, workspace, err);
   }
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
+}
+
+// ---- Allocation-free variant ------------------------------------------------------------------------
+// sk_decode_attention needs a caller-allocated workspace. Some callers cannot allocate device memory
+// at call time: a serving process that reserves its whole device budget at start-up and forbids
+// cudaMalloc afterwards, a host that drives the engine from inside a CUDA graph capture (where
+// cudaMalloc is illegal), or a foreign-language binding that can only hand over buffers it already
+// owns. sk_decode_attention_noalloc serves them: it runs the same kernel with its scratch in a
+// fixed-size array that lives in the library's device image.
+namespace sk {
+namespace decode {
+// 1 MiB per device that loads this library, held until the process exits. The merge counters sit
+// at a fixed place at the end, so calls with different max_len never see each other's partials in
+// their counter slots; the kernel returns every counter to zero before it finishes.
+constexpr size_t kStaticScratchBytes = size_t(1) << 20;
+constexpr size_t kStaticCounterBytes = 4096;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+}  // namespace decode
+}  // namespace sk
+
+namespace {
+std::mutex g_static_mu;
+void* g_static_scratch_ptr[64] = {};
+
+// Device address of g_static_scratch on the current device. The first call on a device looks the
+// address up and zero-fills the array (synchronously), so that first call must come before any
+// stream capture.
+int static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SK_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_scratch_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, sk::decode::g_static_scratch) != cudaSuccess || !p) return SK_ERR_CUDA;
+    if (cudaMemset(p, 0, sk::decode::kStaticScratchBytes) != cudaSuccess) return SK_ERR_CUDA;
+    g_static_scratch_ptr[dev] = p;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return SK_OK;
+}
+}  // namespace
+
+extern "C" int sk_decode_attention_noalloc(const float* qkv, const float* qn, const float* kn, float eps,
+                                           const float* rope, void* Kc, void* Vc, const long long* pos_ptr,
+                                           int pos_add, int max_len, int nq, int nkv, int hd, float* out,
+                                           int cache_dtype, void* stream) {
+  using namespace sk::decode;
+  if (max_len <= 0 || nkv <= 0) return SK_ERR_INVALID_ARG;
+  // partials (o, max/sum) before the counters; the counters always at the array's fixed tail
+  const size_t partial_bytes = ws_bytes(max_len, nkv) - (size_t)nkv * 4 - 256;
+  if (partial_bytes > kStaticScratchBytes - kStaticCounterBytes || (size_t)nkv * 4 > kStaticCounterBytes)
+    return SK_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  int rc = static_scratch(&scratch);
+  if (rc != SK_OK) return rc;
+  char* counters = reinterpret_cast<char*>(scratch) + (kStaticScratchBytes - kStaticCounterBytes);
+  void* base = counters - partial_bytes;  // ws_carve(base) puts the counters exactly at `counters`
+  return sk_decode_attention(qkv, qn, kn, eps, rope, Kc, Vc, pos_ptr, pos_add, max_len, nq, nkv, hd, out, base,
+                             partial_bytes + (size_t)nkv * 4 + 256, cache_dtype, stream);
 }
