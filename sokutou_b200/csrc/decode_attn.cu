@@ -363,10 +363,402 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(
   if (t == 0) ws.cnt[kvh] = 0;  // ready for the next call (and graph replay)
 }
 
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+constexpr int kMaxCluster = 16;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size_reg() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+// Address of `p` (this CTA's shared memory) in the shared memory of cluster rank `rank`.
+__device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+// Bounded wait with cluster-scope acquire: the arrivals came from other CTAs of the cluster.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_dev_error(err, SK_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+template <typename CT>
+struct Vec4;  // four consecutive cache elements as one shared-memory load
+template <>
+struct Vec4<__nv_bfloat16> {
+  static __device__ __forceinline__ float4 ld(const __nv_bfloat16* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+  }
+};
+template <>
+struct Vec4<float> {
+  static __device__ __forceinline__ float4 ld(const float* p) { return *reinterpret_cast<const float4*>(p); }
+};
+
+__device__ __forceinline__ void st_async(uint32_t remote_addr, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(remote_addr), "f"(v),
+               "r"(remote_bar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async4(uint32_t remote_addr, float4 v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   remote_addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
+               : "memory");
+}
+
+constexpr int kThreadsCl = 256;  // 8 warps: two per scheduler, so dependent chains overlap
+constexpr int kPartialBytes = kG * kHD * 4 + kG * 2 * 4;  // one CTA's (o, max, sum) for rank 0
+
+// Cluster variant: one thread-block cluster of CL CTAs per kv head, CL = 16 (or 8 where 16 cannot
+// be co-scheduled). The T keys are cut into CL equal chunks of ceil(T / CL) keys, so every CTA is
+// busy at every T. Each CTA pushes its chunk's partial (o, max, sum) into rank 0's shared memory
+// with st.async, whose completion is counted in bytes on rank 0's mbarrier; rank 0 waits for all
+// CL partials and merges them from its own shared memory. No workspace, no global round trip, no
+// fence or barrier across the cluster on the way out.
+// griddepcontrol.wait precedes every global read (pos, qkv, cache), so under programmatic dependent
+// launch only the CTA set-up overlaps the kernel before.
+template <typename CT>
+__global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
+    const float* __restrict__ qkv, const float* __restrict__ qn, const float* __restrict__ kn, float eps,
+    const float* __restrict__ rope, CT* __restrict__ Kc, CT* __restrict__ Vc, const long long* __restrict__ pos_ptr,
+    int pos_add, int max_len, int nq, int nkv, float* __restrict__ out, int* err) {
+  const int CL = (int)cluster_size_reg();
+  const int rank = (int)cluster_rank();
+  const int chunk_max = (max_len + CL - 1) / CL;
+  extern __shared__ __align__(128) unsigned char dsmem[];
+  CT* Ks = reinterpret_cast<CT*>(dsmem);                               // [chunk_max][kHD]
+  CT* Vs = Ks + (size_t)chunk_max * kHD;                               // [chunk_max][kHD]
+  float* sc = reinterpret_cast<float*>(Vs + (size_t)chunk_max * kHD);  // [chunk_pad][kG]: scores, then p
+  __shared__ __align__(16) float q_s[kG][kHD];
+  __shared__ __align__(16) float kn_s[kHD];
+  __shared__ __align__(16) float vn_s[kHD];
+  __shared__ __align__(16) float o_red[8][kG][kHD];            // PV partials of the 8 key groups
+  __shared__ __align__(16) float all_o[kMaxCluster][kG][kHD];  // rank 0: every CTA's chunk partial o
+  __shared__ __align__(16) float all_ml[kMaxCluster][kG][2];   // rank 0: every CTA's chunk (max, sum)
+  __shared__ float wts[kMaxCluster][kG];                       // rank 0: merge weights
+  __shared__ float den_s[kG];
+  __shared__ float red[8][2];
+  __shared__ float stat[kG][2];
+  __shared__ __align__(8) uint64_t bar;      // the K/V bulk copy
+  __shared__ __align__(8) uint64_t mrg_bar;  // rank 0: CL partials, counted in bytes
+
+  const int kvh = blockIdx.y;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int g_t = t >> 7, d = t & (kHD - 1);  // prologue role: head g_t, dimension d
+  if (t == 0) {
+    mbar_init(&bar, 1);
+    if (rank == 0) mbar_init(&mrg_bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  cluster_arrive_relaxed();  // matched by cluster_wait() before the first push into rank 0
+  if (rank == 0 && t == 0) mbar_arrive_expect_tx(&mrg_bar, (uint32_t)(CL * kPartialBytes));
+  griddep_wait();
+  griddep_launch_dependents();
+  // loads that do not depend on the position go out together with it
+  const float qv = qkv[(size_t)(kvh * kG + g_t) * kHD + d];
+  const float xv = qkv[(size_t)(nq + g_t * nkv) * kHD + (size_t)kvh * kHD + d];  // k (g_t = 0) or v (g_t = 1)
+  const float qn_d = qn[d], kn_d = kn[d];
+  const int pos = (pos_ptr ? (int)pos_ptr[0] : 0) + pos_add;
+  if (pos < 0 || pos >= max_len) {  // every CTA of every cluster reads the same pos: all leave here
+    if (rank == 0 && kvh == 0 && t == 0) set_dev_error(err, SK_DEVERR_POS_RANGE);
+    return;
+  }
+  const int T = pos + 1;
+  const int chunk = (T + CL - 1) / CL;
+  const int s0 = rank * chunk;
+  const int n = max(0, min(chunk, T - s0));  // keys of this CTA (0 for ranks past T)
+  const bool owner = n > 0 && (s0 + n == T);  // holds the new position
+  const int n_ld = owner ? n - 1 : n;
+  const size_t head_base = (size_t)kvh * max_len * kHD;
+  if (t == 0 && n_ld > 0) {
+    const uint32_t bytes = (uint32_t)(n_ld * kHD * sizeof(CT));
+    mbar_arrive_expect_tx(&bar, 2 * bytes);
+    bulk_load(Ks, Kc + head_base + (size_t)s0 * kHD, bytes, &bar);
+    bulk_load(Vs, Vc + head_base + (size_t)s0 * kHD, bytes, &bar);
+  }
+  const float c = rope[(size_t)pos * kHD + (d & 63)];
+  const float s = rope[(size_t)pos * kHD + 64 + (d & 63)];
+
+  // ---- prologue (qwen3/kernels.py:351-380): thread (g_t, d) normalises q head g_t, and the new k
+  // (threads of g_t = 0, owner only); the v of g_t = 1 is stored raw.
+  {
+    const float kv = (owner && g_t == 0) ? xv : 0.f;
+    const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
+    if (lane == 0) {
+      red[w][0] = sq;
+      red[w][1] = sk;
+    }
+    __syncthreads();
+    const int w0 = g_t * 4;  // the 4 warps of this head
+    const float ssq = red[w0][0] + red[w0 + 1][0] + red[w0 + 2][0] + red[w0 + 3][0];
+    const float ssk = red[0][1] + red[1][1] + red[2][1] + red[3][1];
+    q_s[g_t][d] = qv * rsqrtf(ssq / kHD + eps) * qn_d;
+    if (owner && g_t == 0) kn_s[d] = kv * rsqrtf(ssk / kHD + eps) * kn_d;
+    __syncthreads();
+    const float rot = d < 64 ? -q_s[g_t][d + 64] : q_s[g_t][d - 64];
+    const float qr = (q_s[g_t][d] * c + rot * s) * 0.08838834764831845f;  // 1/sqrt(128), qwen3/kernels.py:378
+    float knew = 0.f;
+    if (owner && g_t == 0) {
+      const float rk = d < 64 ? -kn_s[d + 64] : kn_s[d - 64];
+      knew = kn_s[d] * c + rk * s;
+    }
+    __syncthreads();
+    q_s[g_t][d] = qr;
+    if (owner) {
+      if (g_t == 0) {
+        const CT kst = Cache<CT>::st(knew);
+        Kc[head_base + (size_t)pos * kHD + d] = kst;  // append (qwen3/kernels.py:364,366)
+        kn_s[d] = Cache<CT>::ld(&kst);                 // attended as read back from the cache
+      } else {
+        const CT vst = Cache<CT>::st(xv);
+        Vc[head_base + (size_t)pos * kHD + d] = vst;
+        vn_s[d] = Cache<CT>::ld(&vst);
+      }
+    }
+    __syncthreads();
+  }
+  bool ok = true;
+  if (n_ld > 0) ok = mbar_wait(&bar, 0, err);  // on a time-out the output is invalid (error word set)
+
+  // ---- scores, 64 keys per pass: warp w owns keys [8w, 8w+8) of the pass; lane owns 4 dims
+  {
+    float4 qa[kG];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) qa[g] = *reinterpret_cast<const float4*>(&q_s[g][4 * lane]);
+    const float4 knew4 = *reinterpret_cast<const float4*>(&kn_s[4 * lane]);
+    for (int base = 0; base < n; base += 64) {
+      float part[kG * 8];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int j = base + 8 * w + jj;
+        const float4 k4 = (ok && j < n_ld) ? Vec4<CT>::ld(Ks + (size_t)j * kHD + 4 * lane) : knew4;
+#pragma unroll
+        for (int g = 0; g < kG; ++g)
+          part[g * 8 + jj] = qa[g].x * k4.x + qa[g].y * k4.y + qa[g].z * k4.z + qa[g].w * k4.w;
+      }
+      // reduce-scatter of 16 values over lane bits 4..1, then a plain sum over bit 0
+#pragma unroll
+      for (int off = 16, m = 16; off >= 2; off >>= 1, m >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < m / 2; ++i) {
+          const float send = upper ? part[i] : part[i + m / 2];
+          const float keep = upper ? part[i + m / 2] : part[i];
+          part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      part[0] += __shfl_xor_sync(0xffffffffu, part[0], 1);
+      // lane l now holds value index (l >> 1): head (l >> 4), key (l >> 1) & 7
+      const int g = lane >> 4, j = base + 8 * w + ((lane >> 1) & 7);
+      if ((lane & 1) == 0 && j < n) sc[j * kG + g] = part[0];
+    }
+  }
+  __syncthreads();
+  // ---- chunk softmax: warp g handles head g
+  if (w < kG) {
+    const int g = w;
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[j * kG + g]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const float e = expf(sc[j * kG + g] - m);
+      sc[j * kG + g] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      stat[g][0] = m;  // -inf for a CTA with no keys
+      stat[g][1] = l;
+    }
+  }
+  __syncthreads();
+  // ---- PV: thread owns dims [4*(t%32), +4) over keys j = w, w + 8, ...
+  {
+    const int dq = 4 * lane;
+    float4 acc[kG];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 vnew4 = *reinterpret_cast<const float4*>(&vn_s[dq]);
+    for (int j = w; j < n; j += 8) {
+      const float4 v4 = (ok && j < n_ld) ? Vec4<CT>::ld(Vs + (size_t)j * kHD + dq) : vnew4;
+      const float2 p = *reinterpret_cast<const float2*>(&sc[j * kG]);
+      acc[0].x += p.x * v4.x;
+      acc[0].y += p.x * v4.y;
+      acc[0].z += p.x * v4.z;
+      acc[0].w += p.x * v4.w;
+      acc[1].x += p.y * v4.x;
+      acc[1].y += p.y * v4.y;
+      acc[1].z += p.y * v4.z;
+      acc[1].w += p.y * v4.w;
+    }
+#pragma unroll
+    for (int g = 0; g < kG; ++g) *reinterpret_cast<float4*>(&o_red[w][g][dq]) = acc[g];
+  }
+  __syncthreads();
+  // ---- push this chunk's partial into rank 0 (st.async, completion counted on rank 0's barrier)
+  cluster_wait();  // rank 0's barrier is initialised
+  {
+    const uint32_t rbar = mapa(&mrg_bar, 0);
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v += o_red[i][g_t][d];
+    st_async(mapa(&all_o[rank][g_t][d], 0), v, rbar);
+    if (t < kG * 2) st_async(mapa(&all_ml[rank][t >> 1][t & 1], 0), stat[t >> 1][t & 1], rbar);
+  }
+  if (rank == 0) {
+    // block-uniform: a time-out seen by any thread skips the merge for the whole CTA
+    const bool got = __syncthreads_and(mbar_wait_cluster(&mrg_bar, 0, err)) != 0;
+    if (got) {
+      if (t < kMaxCluster * kG) {  // weight of each chunk, in parallel
+        const int r = t >> 1, g = t & 1;
+        float M = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kMaxCluster; ++i)
+          if (i < CL) M = fmaxf(M, all_ml[i][g][0]);
+        wts[r][g] = (r < CL && all_ml[r][g][1] > 0.f) ? expf(all_ml[r][g][0] - M) : 0.f;
+      }
+      __syncthreads();
+      if (t < kG) {
+        float dn = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxCluster; ++r)
+          if (r < CL) dn += wts[r][t] * all_ml[r][t][1];
+        den_s[t] = dn;
+      }
+      __syncthreads();
+      float num = 0.f;
+#pragma unroll
+      for (int r = 0; r < kMaxCluster; ++r)
+        if (r < CL) num += wts[r][g_t] * all_o[r][g_t][d];
+      out[(size_t)(kvh * kG + g_t) * kHD + d] = num / den_s[g_t];
+    }
+  }
+  if (!ok && t == 0) mbar_wait(&bar, 0, err);
+}
+
 }  // namespace decode
 }  // namespace sk
 
 using namespace sk;
+
+
+namespace sk {
+namespace decode {
+
+// Cluster size usable on this device for a kernel needing `smem` bytes: 16 when nkv clusters of
+// 16 fit at once, else 8, else 0 (cached per device, dtype and shared-memory size).
+template <typename CT>
+static int cluster_size(int nkv, size_t smem) {
+  static std::mutex mu;
+  static int cached_cl[64][2] = {};
+  static size_t cached_smem[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  const int ti = sizeof(CT) == 2 ? 0 : 1;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cached_smem[dev][ti] == smem && cached_cl[dev][ti] != 0) return cached_cl[dev][ti];
+  auto kfn = decode_attn_cluster_kernel<CT>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+  cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  int chosen = 0;
+  for (int cl : {16, 8}) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl, nkv);
+    cfg.blockDim = dim3(kThreadsCl);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) == cudaSuccess && n >= nkv) {
+      chosen = cl;
+      break;
+    }
+    cudaGetLastError();  // clear a refused query
+  }
+  cached_cl[dev][ti] = chosen;
+  cached_smem[dev][ti] = smem;
+  return chosen;
+}
+
+template <typename CT>
+static int launch_cluster(const float* qkv, const float* qn, const float* kn, float eps, const float* rope, void* Kc,
+                          void* Vc, const long long* pos_ptr, int pos_add, int max_len, int nq, int nkv, float* out,
+                          int* err, cudaStream_t st) {
+  // the shared memory of the largest chunk decides whether one cluster per kv head can hold T = max_len
+  for (int cl : {16, 8}) {
+    const int chunk_max = (max_len + cl - 1) / cl;
+    const size_t smem = 2 * (size_t)chunk_max * kHD * sizeof(CT) + (size_t)kG * ((chunk_max + 63) & ~63) * 4;
+    if (smem > 160 * 1024) continue;
+    const int use = cluster_size<CT>(nkv, smem);
+    if (use != cl) continue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl, nkv);
+    cfg.blockDim = dim3(kThreadsCl);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, decode_attn_cluster_kernel<CT>, qkv, qn, kn, eps, rope, reinterpret_cast<CT*>(Kc),
+                           reinterpret_cast<CT*>(Vc), pos_ptr, pos_add, max_len, nq, nkv, out, err) != cudaSuccess)
+      return SK_ERR_CUDA;
+    return SK_OK;
+  }
+  return SK_ERR_UNSUPPORTED;
+}
+
+}  // namespace decode
+}  // namespace sk
 
 extern "C" size_t sk_decode_workspace_bytes(int max_len, int nq, int nkv, int hd, int cache_dtype) {
   (void)nq;
@@ -395,6 +787,14 @@ extern "C" int sk_decode_attention(const float* qkv, const float* qn, const floa
   int* err = sk_error_word_ptr();
   if (!err) return SK_ERR_CUDA;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (max_len > decode::kChunk) {
+    rc = cache_dtype == SK_BF16
+             ? decode::launch_cluster<__nv_bfloat16>(qkv, qn, kn, eps, rope, Kc, Vc, pos_ptr, pos_add, max_len, nq,
+                                                      nkv, out, err, st)
+             : decode::launch_cluster<float>(qkv, qn, kn, eps, rope, Kc, Vc, pos_ptr, pos_add, max_len, nq, nkv,
+                                             out, err, st);
+    if (rc != SK_ERR_UNSUPPORTED) return rc;  // else: too long for one cluster, use the workspace kernel
+  }
   dim3 grid(nsplit, nkv), block(decode::kThreads);
   if (cache_dtype == SK_BF16) {
     const size_t smem = 2 * decode::kChunk * decode::kHD * sizeof(__nv_bfloat16);

@@ -25,6 +25,8 @@ CASES = {
     "dit_c2_b3": ("dit", W.C2, 3), "dit_c2_b1": ("dit", W.C2, 1),
     "decode_T128": ("decode", 128, None), "decode_T512": ("decode", 512, None),
     "decode_T1120": ("decode", 1120, None), "decode_T1500": ("decode", 1500, None),
+    # calibration: what a chain of dependent kernels costs on this GPU without any attention work
+    "calib_tiny": ("calib", 0, None), "calib_copy_4.6MB": ("calib", 4616192, None),
 }
 
 
@@ -60,16 +62,34 @@ def decode_case(T, sets, dev):
     return fns, s.layer_bytes(T), "byte"
 
 
+def calib_case(nbytes, sets, dev):
+    """A dependent chain of torch kernels: a one-element add (launch floor), or a device copy of
+    `nbytes` (twice that moved) over 16 rotating buffer pairs so the copies miss L2."""
+    if nbytes == 0:
+        x = torch.zeros(1, device=dev)
+        return [lambda: x.add_(1.0)], 1, "byte"
+    n = nbytes // 2
+    bufs = [(torch.randn(n, device=dev).bfloat16(), torch.empty(n, device=dev, dtype=torch.bfloat16))
+            for _ in range(16)]
+    return [lambda a=a, b=b: b.copy_(a) for a, b in bufs], 2 * nbytes, "byte"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", required=True, choices=sorted(CASES))
     ap.add_argument("--reps", type=int, default=50)
     ap.add_argument("--sets", type=int, default=4)
     ap.add_argument("--graph", action="store_true")
+    ap.add_argument("--warm-ms", type=float, default=300.0, help="busy time before timing (clock ramp-up)")
     a = ap.parse_args()
     dev = torch.device("cuda:0")
     kind, x, B = CASES[a.case]
-    fns, work, unit = dit_case(x, B, a.sets, dev) if kind == "dit" else decode_case(x, a.sets, dev)
+    if kind == "dit":
+        fns, work, unit = dit_case(x, B, a.sets, dev)
+    elif kind == "decode":
+        fns, work, unit = decode_case(x, a.sets, dev)
+    else:
+        fns, work, unit = calib_case(x, a.sets, dev)
     for f in fns:
         f()
     torch.cuda.synchronize()
@@ -87,6 +107,11 @@ def main():
         run = gr.replay
         run()
     torch.cuda.synchronize()
+    import time
+    t_end = time.perf_counter() + a.warm_ms / 1e3
+    while time.perf_counter() < t_end:
+        run()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     run()

@@ -95,6 +95,26 @@ def test_against_oracle(cuda, T, cache):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("cache", ["bf16", "f32"])
+def test_long_cache_uses_workspace_kernel(cuda, cache):
+    """max_len beyond one cluster's shared memory: the split-KV workspace kernel takes the call."""
+    max_len = 6144 if cache == "bf16" else 3072
+    T = max_len - 7
+    nq, nkv = 16, 8
+    Kc, Vc, qkv, qn, kn, rope = _random_case(cuda, T, max_len, cache, seed=99)
+    Kh, Vh = host(Kc).astype(np.float64), host(Vc).astype(np.float64)
+    ref = Q.decode_step(qkv, qn, kn, 1e-6, rope, Kh, Vh, T - 1, nq, nkv, cache)
+    f = lambda a: torch.from_numpy(a).to(cuda).contiguous()
+    out = torch.empty(nq * 128, device=cuda)
+    ws = ops.decode_workspace(max_len, nq, nkv, cuda, cache_dtype=Kc.dtype)
+    pos = torch.tensor([T - 1], device=cuda, dtype=torch.int64)
+    for _ in range(2):  # the merge counters are back at zero for the second call
+        ops.decode_attention(f(qkv), f(qn), f(kn), 1e-6, f(rope), Kc, Vc, pos, 0, max_len, nq, nkv, out, ws)
+        torch.cuda.synchronize()
+        assert rel_l2(host(out), ref) < (FP32_TOL if cache == "f32" else BF16_TOL)
+    assert ops.device_error() == 0
+
+
 def test_workspace_counters_return_to_zero(cuda):
     max_len, nq, nkv = 1536, 16, 8
     Kc, Vc, qkv, qn, kn, rope = _random_case(cuda, 1000, max_len, "bf16", seed=1)

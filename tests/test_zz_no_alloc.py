@@ -5,7 +5,9 @@ split-KV scratch in a fixed array inside the library instead of a caller workspa
 
 Checked through the C ABI against sk_decode_attention on identical inputs, two calls in a row with
 different cache lengths (so the second call reuses the scratch the first one left behind), within the
-decode tolerance of the other tests (relative L2 <= 1e-5). Collected last so that a failure here
+decode tolerance of the other tests (relative L2 <= 1e-5). The cache lengths are long enough that the
+split-KV path with the scratch runs (shorter caches are merged inside one thread-block cluster and
+need no scratch at all). Collected last so that a failure here
 leaves every other test already run.
 """
 
@@ -42,7 +44,8 @@ def test_noalloc_matches_workspace_entry_point(cuda, cache_dtype):
     code = 0 if cache_dtype == torch.bfloat16 else 1
     stream = torch.cuda.current_stream().cuda_stream
     nq, nkv = 16, 8
-    for call, (max_len, T) in enumerate([(1536, 1120), (512, 300)]):
+    long_len = 6144 if cache_dtype == torch.bfloat16 else 3072
+    for call, (max_len, T) in enumerate([(long_len, long_len - 100), (long_len - 256, 1500)]):
         Kc, Vc, qkv, qn, kn, rope, pos = _case(cuda, max_len, T, cache_dtype, seed=10 + call)
         Kc2, Vc2 = Kc.clone(), Vc.clone()
         ref = torch.empty(nq * 128, device=cuda)
