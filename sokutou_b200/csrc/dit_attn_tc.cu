@@ -1,22 +1,25 @@
 // DiT attention, bf16 mode, on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
 //
 // Replaces F.scaled_dot_product_attention(q, k, v, attn_mask=bias) at engine/fused.py:295.
-// One CTA computes a 128-row query tile of one (batch, head) against all K = Lk + S keys:
+// One CTA computes a 128-row query tile of one (batch, head) against all K = Lk + S keys, in key
+// tiles of 128:
 //
-//   warp 4 (one lane)  TMA producer: Q once, then K and V tiles of 128 keys into two rings of
-//                      NSK and NSV slots. The rings are released independently: a K slot frees as
-//                      soon as S = Q·Kᵀ has consumed it, a V slot when O += P·V has. The producer
-//                      polls both rings, so neither blocks the other.
-//                      Latent keys come from (B, H, Lk, hd); conditioning keys straight from their
-//                      batch-shared (S, H, hd) buffer — no per-CFG-branch copy.
-//   warp 5 (one lane)  MMA issuer: S_j = Q·K_jᵀ into one of two TMEM S buffers (128 fp32 columns
-//                      each), issued one tile ahead, then O += P_j·V_j into the TMEM O accumulator.
-//   warps 0-3          softmax: thread t owns query row t = TMEM lane t. It loads its S row
-//                      (tcgen05.ld), applies scale and key bias with packed fp32x2 FMAs, keeps a
-//                      running max in the log2 domain, writes P_j (bf16) into a 128B-swizzled
-//                      shared-memory tile, and rescales O in TMEM only when its max grew by more
-//                      than 2^8 (exact either way: numerator and denominator share the stale max).
-//                      Epilogue: O / l -> bf16 -> y (B, L, H, hd).
+//   warp 8 (one lane)  TMA producer: Q once, then K and V tiles into two rings of NSK and NSV slots,
+//                      released independently (a K slot as soon as S = Q·Kᵀ has consumed it, a V slot
+//                      when O += P·V has); the producer polls both rings. Latent keys come from
+//                      (B, H, Lk, hd), conditioning keys straight from their batch-shared (S, H, hd)
+//                      buffer — no per-CFG-branch copy.
+//   warp 9 (one lane)  MMA issuer: S_j = Q·K_jᵀ into TMEM buffer S[j % 2], O_w += P_j·V_j into the
+//                      TMEM accumulator O[j % 2], two tiles in flight.
+//   warps 0-3, 4-7     two softmax warpgroups; warpgroup w takes the tiles j with j % 2 == w, so two
+//                      tiles' softmax run at once. Thread r of a warpgroup owns query row r (TMEM lane
+//                      r): it loads its S row (tcgen05.ld), applies scale and key bias (prefetched one
+//                      tile ahead) with packed fp32x2 FMAs, keeps a running max in the log2 domain,
+//                      writes P (bf16) as a 128B-swizzled shared-memory tile, and rescales its O row in
+//                      TMEM only when the max grew by more than 2^8 (exact either way: numerator and
+//                      denominator share the stale max).
+//   epilogue           the two (max, sum, O) partials of each row are merged, O / l -> bf16 ->
+//                      y (B, L, H, hd); warpgroup w writes half of the hd columns.
 // Every thread executes griddepcontrol.wait before touching global memory, so with programmatic
 // dependent launch a kernel's set-up (barriers, TMEM, descriptor prefetch) overlaps the tail of
 // the kernel before it while every input read still follows that kernel's completion.
@@ -26,7 +29,7 @@
 //   K [128 keys][hd]   K-major B of S
 //   P [128 rows][128]  K-major A of O = P·V        (keys split in 64-element chunks)
 //   V [128 keys][hd]   MN-major B of O (hd contiguous), LBO = chunk stride, SBO = 8 rows
-// TMEM: columns [0,128) S0, [128,256) S1, [256, 256+hd) O; 512 columns allocated.
+// TMEM: columns [0,128) S0, [128,256) S1, [256, 256+hd) O0, [256+hd, 256+2hd) O1; 512 allocated.
 #include <mutex>
 
 #include "sk_common.cuh"
@@ -35,7 +38,12 @@ namespace sk {
 namespace dit {
 
 constexpr int kBM = 128, kBN = 128;
-constexpr int kThreadsTC = 192;
+constexpr int kThreadsTC = 384;  // 2 softmax warpgroups + a warpgroup holding the producer and MMA warps
+constexpr int kWarpProducer = 8, kWarpMma = 9;
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512); the producer/MMA
+// warpgroup gives registers back, the softmax warpgroups take them: 256 x 232 + 128 x 40 = 64512.
+constexpr int kLaunchRegs = 168, kSoftmaxRegs = 232, kControlRegs = 40;
+static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreadsTC * kLaunchRegs, "register split over budget");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
 
@@ -43,16 +51,16 @@ template <int HD>
 struct TcCfg;
 template <>
 struct TcCfg<64> {  // 16 + 4*16 + 4*16 + 2*32 = 208 KB
-  static constexpr int NSK = 4, NSV = 4, NP = 2;
+  static constexpr int NSK = 4, NSV = 4;
 };
 template <>
-struct TcCfg<128> {  // 32 + 3*32 + 2*32 + 1*32 = 224 KB
-  static constexpr int NSK = 3, NSV = 2, NP = 1;
+struct TcCfg<128> {  // 32 + 2*32 + 2*32 + 2*32 = 224 KB
+  static constexpr int NSK = 2, NSV = 2;
 };
 
 template <int HD>
 struct TcLayout {
-  static constexpr int NSK = TcCfg<HD>::NSK, NSV = TcCfg<HD>::NSV, NP = TcCfg<HD>::NP;
+  static constexpr int NSK = TcCfg<HD>::NSK, NSV = TcCfg<HD>::NSV;
   static constexpr int NCH = HD / 64;              // 64-element (128-byte) chunks per row
   static constexpr int Q_BYTES = kBM * HD * 2;
   static constexpr int KV_BYTES = kBN * HD * 2;
@@ -60,15 +68,20 @@ struct TcLayout {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + NSK * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + NSV * KV_BYTES;
-  static constexpr int OFF_BIAS = OFF_P + NP * P_BYTES;  // float [2][kBN]
-  static constexpr int OFF_BAR = OFF_BIAS + 2 * kBN * 4;
-  // q_full, k_full/k_empty[NSK], v_full/v_empty[NSV], s_full[2], s_free[2], p_full[NP], o_done[NP], mma_done
-  static constexpr int NBAR = 1 + 2 * NSK + 2 * NSV + 4 + 2 * NP + 1;
+  static constexpr int OFF_P = OFF_V + NSV * KV_BYTES;       // one P tile per softmax warpgroup
+  // float [2 wg][2 buf][kBN] key bias; after its tile loop a warpgroup reuses its own 2*kBN floats
+  // for the (max, sum) of its kBM rows that the epilogue exchanges
+  static constexpr int OFF_BIAS = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_BAR = OFF_BIAS + 4 * kBN * 4;
+  // q_full, k_full/k_empty[NSK], v_full/v_empty[NSV], s_full[2], s_free[2], p_full[2], o_done[2], mma_done
+  static constexpr int NBAR = 1 + 2 * NSK + 2 * NSV + 8 + 1;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
-  static constexpr int SMEM_ALLOC = BYTES + 1024;  // slack to align the base to 1024
+  // The dynamic shared-memory base is 1024-byte aligned on sm_100 (checked at run time); the
+  // 128B-swizzled tiles need that alignment.
+  static constexpr int SMEM_ALLOC = BYTES;
   static_assert(SMEM_ALLOC <= 232448, "shared memory over the 227 KB per-CTA limit");
+  static_assert(2 * kBM <= 2 * kBN, "the (max, sum) exchange must fit a warpgroup's bias area");
 };
 
 struct TcParams {
@@ -88,7 +101,30 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 }
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// Key bias of column `col` of key tile j in the log2 domain; -inf past the end of its segment.
+__device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloat16* bias, int b, int j, int n_lat,
+                                           int col) {
+  int key = -1;
+  if (j < n_lat) {
+    const int kk = j * kBN + col;
+    key = kk < prm.Lk ? kk : -1;
+  } else {
+    const int kk = (j - n_lat) * kBN + col;
+    key = kk < prm.S ? prm.Lk + kk : -1;
+  }
+  if (key < 0) return -INFINITY;
+  return bias ? __bfloat162float(bias[(size_t)b * prm.bias_bs + key]) * kLog2e : 0.f;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kThreadsTC, 1)
@@ -96,10 +132,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
                    const __grid_constant__ CUtensorMap tmVc, const TcParams prm) {
   using Ly = TcLayout<HD>;
-  constexpr int NSK = Ly::NSK, NSV = Ly::NSV, NP = Ly::NP;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int NSK = Ly::NSK, NSV = Ly::NSV;
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {  // uniform for the CTA, before any barrier: report and leave
+    if (threadIdx.x == 0) set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
+    return;
+  }
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly::OFF_BAR);
   uint64_t* q_full = bars;
@@ -110,8 +149,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* s_full = v_empty + NSV;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
-  uint64_t* o_done = p_full + NP;
-  uint64_t* mma_done = o_done + NP;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* mma_done = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::OFF_TMEM);
   float* bias_s = reinterpret_cast<float*>(smem + Ly::OFF_BIAS);
 
@@ -133,15 +172,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
-    }
-    for (int i = 0; i < NP; ++i) {
       mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(mma_done, 1);
     fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kWarpProducer && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
@@ -150,7 +187,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       tma_prefetch_desc(&tmVc);
     }
   }
-  if (warp == 5) {
+  if (warp == kWarpMma) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -162,9 +199,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   griddep_wait();
   griddep_launch_dependents();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS0 = tmem, tO = tmem + 256;
-
-  if (warp == 4) {
+  const uint32_t tS = tmem, tO = tmem + 256;  // S[w] at tS + 128 w, O[w] at tO + HD w
+  if (warp >= 8) {
+  setmaxnreg_dec<kControlRegs>();
+  if (warp == kWarpProducer) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const int bh = b * prm.H + h;
@@ -173,7 +211,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
       for (int c = 0; c < Ly::NCH; ++c)
         tma_load_3d(smem + Ly::OFF_Q + c * (kBM * 128), &tmQ, q_full, c * 64, q0, bh);
-      // K_j and V_j are issued as soon as their ring slot is free, each ring on its own.
       int jk = 0, jv = 0;
       bool ok = true;
       const uint64_t t0 = globaltimer_ns();
@@ -220,7 +257,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int j = (jk > NSK ? jk - NSK : 0); j < jk; ++j) mbar_wait(&k_full[j % NSK], (j / NSK) & 1, prm.err);
       for (int j = (jv > NSV ? jv - NSV : 0); j < jv; ++j) mbar_wait(&v_full[j % NSV], (j / NSV) & 1, prm.err);
     }
-  } else if (warp == 5) {
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(kBM, kBN, 0, 0);
@@ -236,7 +273,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
           const uint32_t offk = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-          tc_mma_ss(tS0 + sb * 128, smem_desc_sw128(aQ + off, 16, 1024),
+          tc_mma_ss(tS + sb * 128, smem_desc_sw128(aQ + off, 16, 1024),
                     smem_desc_sw128(aK + s * Ly::KV_BYTES + offk, 16, 1024), idS, kk > 0);
         }
         tc_commit(&s_full[sb]);
@@ -244,11 +281,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         return true;
       };
       if (ok) ok = issue_s(0);
+      if (ok && ntiles > 1) ok = issue_s(1);
       for (int j = 0; j < ntiles && ok; ++j) {
-        if (j + 1 < ntiles) ok = issue_s(j + 1);
-        if (!ok) break;
-        const int sv = j % NSV, pb = j % NP;
-        if (!mbar_wait(&p_full[pb], (j / NP) & 1, prm.err) || !mbar_wait(&v_full[sv], (j / NSV) & 1, prm.err)) {
+        const int sv = j % NSV, w = j & 1;
+        if (!mbar_wait(&p_full[w], (j >> 1) & 1, prm.err) || !mbar_wait(&v_full[sv], (j / NSV) & 1, prm.err)) {
           ok = false;
           break;
         }
@@ -256,85 +292,90 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint32_t offp = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          tc_mma_ss(tO, smem_desc_sw128(aP + pb * Ly::P_BYTES + offp, 16, 1024),
-                    smem_desc_sw128(aV + sv * Ly::KV_BYTES + kk * 2048, kBN * 128, 1024), idO, (j > 0 || kk > 0));
+          tc_mma_ss(tO + w * HD, smem_desc_sw128(aP + w * Ly::P_BYTES + offp, 16, 1024),
+                    smem_desc_sw128(aV + sv * Ly::KV_BYTES + kk * 2048, kBN * 128, 1024), idO, (j >= 2 || kk > 0));
         }
-        tc_commit(&o_done[pb]);
+        tc_commit(&o_done[w]);
         tc_commit(&v_empty[sv]);
+        if (j + 2 < ntiles) ok = issue_s(j + 2);
       }
       tc_commit(mma_done);
       mbar_wait(mma_done, 0, prm.err);
     }
+  }
   } else {
-    // ------------------------------------------------------------------ softmax warpgroup (warps 0-3)
-    const int row = threadIdx.x;  // TMEM lane == query row within the tile
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // ------------------------------------------------------------------ softmax warpgroups (warps 0-7)
+    setmaxnreg_inc<kSoftmaxRegs>();
+    const int wg = warp >> 2;
+    const int row = threadIdx.x & 127;  // TMEM lane == query row within the tile
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(prm.bias);
-    uint8_t* prow_base = smem + Ly::OFF_P + row * 128;
+    uint8_t* prow = smem + Ly::OFF_P + wg * Ly::P_BYTES + row * 128;
     const float2 sl2 = make_float2(prm.scale_log2, prm.scale_log2);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles && ok; ++j) {
-      const int sb = j & 1;
-      // key bias of this tile, log2 domain; -inf for keys past the end of their segment
-      {
-        int key = -1;
-        if (j < n_lat) {
-          const int kk = j * kBN + row;
-          key = kk < prm.Lk ? kk : -1;
-        } else {
-          const int kk = (j - n_lat) * kBN + row;
-          key = kk < prm.S ? prm.Lk + kk : -1;
-        }
-        float bv = -INFINITY;
-        if (key >= 0) bv = bias ? __bfloat162float(bias[(size_t)b * prm.bias_bs + key]) * kLog2e : 0.f;
-        bias_s[sb * kBN + row] = bv;
-      }
-      named_bar_sync(1, 128);
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, prm.err)) {
+    float bnext = (wg < ntiles) ? tile_bias(prm, bias, b, wg, n_lat, row) : 0.f;
+    for (int j = wg; j < ntiles && ok; j += 2) {
+      const int it = j >> 1;  // this warpgroup's tile count so far
+      float* bt = bias_s + (wg * 2 + (it & 1)) * kBN;
+      bt[row] = bnext;
+      if (j + 2 < ntiles) bnext = tile_bias(prm, bias, b, j + 2, n_lat, row);  // lands during this tile
+      named_bar_sync(1 + wg, 128);
+      if (!mbar_wait(&s_full[wg], it & 1, prm.err)) {
         ok = false;
         break;
       }
       tc_fence_after();
       float x[kBN];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS0 + sb * 128 + lane_off + c * 32, x + c * 32);
+      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + wg * 128 + lane_off + c * 32, x + c * 32);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-      // t = s·scale·log2e + bias·log2e, packed two at a time; running row max with 3-input max
-      float mt = -INFINITY;
-      const float4* bt4 = reinterpret_cast<const float4*>(bias_s + sb * kBN);
+      mbar_arrive(&s_free[wg]);
+      // t = s·scale·log2e + bias·log2e, packed two at a time; row max over four independent chains
+      float mt0 = -INFINITY, mt1 = -INFINITY, mt2 = -INFINITY, mt3 = -INFINITY;
+      const float4* bt4 = reinterpret_cast<const float4*>(bt);
 #pragma unroll
-      for (int c = 0; c < kBN; c += 4) {
-        const float4 bb = bt4[c >> 2];
-        float2 t0 = __ffma2_rn(make_float2(x[c], x[c + 1]), sl2, make_float2(bb.x, bb.y));
-        float2 t1 = __ffma2_rn(make_float2(x[c + 2], x[c + 3]), sl2, make_float2(bb.z, bb.w));
+      for (int c = 0; c < kBN; c += 8) {
+        const float4 ba = bt4[c >> 2], bb = bt4[(c >> 2) + 1];
+        const float2 t0 = __ffma2_rn(make_float2(x[c], x[c + 1]), sl2, make_float2(ba.x, ba.y));
+        const float2 t1 = __ffma2_rn(make_float2(x[c + 2], x[c + 3]), sl2, make_float2(ba.z, ba.w));
+        const float2 t2 = __ffma2_rn(make_float2(x[c + 4], x[c + 5]), sl2, make_float2(bb.x, bb.y));
+        const float2 t3 = __ffma2_rn(make_float2(x[c + 6], x[c + 7]), sl2, make_float2(bb.z, bb.w));
         x[c] = t0.x;
         x[c + 1] = t0.y;
         x[c + 2] = t1.x;
         x[c + 3] = t1.y;
-        mt = max3(mt, max3(t0.x, t0.y, t1.x), t1.y);
+        x[c + 4] = t2.x;
+        x[c + 5] = t2.y;
+        x[c + 6] = t3.x;
+        x[c + 7] = t3.y;
+        mt0 = max3(mt0, t0.x, t0.y);
+        mt1 = max3(mt1, t1.x, t1.y);
+        mt2 = max3(mt2, t2.x, t2.y);
+        mt3 = max3(mt3, t3.x, t3.y);
       }
+      const float mt = fmaxf(fmaxf(mt0, mt1), fmaxf(mt2, mt3));
       const float m_new = fmaxf(m_run, mt);
       const bool want = m_new > m_run + kRescaleLog2;  // false while every key seen is masked
+      // P tile and O rows of this warpgroup were last used by PV_{j-2}
+      if (j >= 2 && !mbar_wait(&o_done[wg], ((j - 2) >> 1) & 1, prm.err)) {
+        ok = false;
+        break;
+      }
       if (__any_sync(0xffffffffu, want)) {
         // warp-uniform: every lane of the warp moves to its exact current max
         const float alpha = (m_new == -INFINITY) ? 1.f : ex2_approx(m_run - m_new);
-        if (j > 0) {
-          if (!mbar_wait(&o_done[(j - 1) % NP], ((j - 1) / NP) & 1, prm.err)) {
-            ok = false;
-            break;
-          }
+        if (j >= 2) {
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
             float ov[32];
-            tmem_ld32(tO + lane_off + c * 32, ov);
+            tmem_ld32(tO + wg * HD + lane_off + c * 32, ov);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(tO + lane_off + c * 32, ov);
+            tmem_st32(tO + wg * HD + lane_off + c * 32, ov);
           }
           tmem_wait_st();
         }
@@ -343,21 +384,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       const float2 nm = make_float2(-m_use, -m_use);
-      // P buffer (j % NP) was last read by PV_{j-NP}
-      if (j >= NP && !mbar_wait(&o_done[j % NP], ((j / NP) - 1) & 1, prm.err)) {
-        ok = false;
-        break;
-      }
-      float2 lsum = make_float2(0.f, 0.f);
-      uint8_t* prow = prow_base + (j % NP) * Ly::P_BYTES;
+      float2 ls0 = make_float2(0.f, 0.f), ls1 = ls0;
 #pragma unroll
       for (int u = 0; u < kBN / 8; ++u) {  // 16 units of 8 keys = 16 bytes
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 d = __fadd2_rn(make_float2(x[8 * u + 2 * e], x[8 * u + 2 * e + 1]), nm);
-          const float2 p = make_float2(ex2_approx(d.x), ex2_approx(d.y));
-          lsum = __fadd2_rn(lsum, p);
+          const float2 dd = __fadd2_rn(make_float2(x[8 * u + 2 * e], x[8 * u + 2 * e + 1]), nm);
+          const float2 p = make_float2(ex2_approx(dd.x), ex2_approx(dd.y));
+          if (e & 1)
+            ls1 = __fadd2_rn(ls1, p);
+          else
+            ls0 = __fadd2_rn(ls0, p);
           const __nv_bfloat162 pb2 = __floats2bfloat162_rn(p.x, p.y);
           pk[e] = *reinterpret_cast<const uint32_t*>(&pb2);
         }
@@ -367,32 +405,63 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                      "r"(pk[2]), "r"(pk[3])
                      : "memory");
       }
-      l_run += lsum.x + lsum.y;
+      l_run += (ls0.x + ls0.y) + (ls1.x + ls1.y);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full[j % NP]);
+      mbar_arrive(&p_full[wg]);
     }
-    // ---- epilogue: y = O / l
-    if (ok && mbar_wait(&o_done[(ntiles - 1) % NP], ((ntiles - 1) / NP) & 1, prm.err)) {
+    // ---- epilogue: merge the two warpgroups' (max, sum, O) for each row; wg writes half the columns
+    named_bar_sync(1 + wg, 128);  // this warpgroup is done reading its bias area
+    {
+      float* ml = bias_s + wg * 2 * kBN;  // [kBM][2]
+      ml[row * 2] = m_run;
+      ml[row * 2 + 1] = l_run;
+    }
+    named_bar_sync(3, 256);
+    bool okk = ok;
+    for (int w = 0; w < 2 && okk; ++w) {  // both accumulators complete (the last PV of each)
+      const int jl = ((ntiles - 1 - w) >> 1) * 2 + w;
+      if (jl < ntiles && jl >= 0) okk = mbar_wait(&o_done[w], (jl >> 1) & 1, prm.err);
+    }
+    okk = __all_sync(0xffffffffu, okk);
+    if (okk) {
       tc_fence_after();
-      const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
+      const float m0 = bias_s[row * 2], l0 = bias_s[row * 2 + 1];
+      const float m1 = bias_s[2 * kBN + row * 2], l1 = bias_s[2 * kBN + row * 2 + 1];
+      const float m = fmaxf(m0, m1);
+      const float a0 = (l0 > 0.f) ? ex2_approx(m0 - m) : 0.f;
+      const float a1 = (l1 > 0.f) ? ex2_approx(m1 - m) : 0.f;
+      const float l = a0 * l0 + a1 * l1;
+      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      const float c0 = a0 * inv, c1 = a1 * inv;
       const int qi = q0 + row;
       __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(prm.y) + (((size_t)b * prm.L + qi) * prm.H + h) * HD;
+      constexpr int NC = HD / 64;  // 32-column chunks per warpgroup half
+      float o0[NC][32], o1[NC][32];
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        float ov[32];
-        tmem_ld32(tO + lane_off + c * 32, ov);
-        tmem_wait_ld();
-        if (qi < prm.L) {
+      for (int c = 0; c < NC; ++c) {
+        const uint32_t col = wg * (HD / 2) + c * 32;
+        tmem_ld32(tO + lane_off + col, o0[c]);
+        tmem_ld32(tO + HD + lane_off + col, o1[c]);
+      }
+      tmem_wait_ld();
+      if (qi < prm.L) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const int col = wg * (HD / 2) + c * 32;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint32_t pk[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 v2 = __floats2bfloat162_rn(ov[8 * u + 2 * e] * inv, ov[8 * u + 2 * e + 1] * inv);
+              const int i0 = 8 * u + 2 * e;
+              // c1 == 0 when the second accumulator never ran: do not touch its contents
+              const float y0 = o0[c][i0] * c0 + (c1 != 0.f ? o1[c][i0] * c1 : 0.f);
+              const float y1 = o0[c][i0 + 1] * c0 + (c1 != 0.f ? o1[c][i0 + 1] * c1 : 0.f);
+              const __nv_bfloat162 v2 = __floats2bfloat162_rn(y0, y1);
               pk[e] = *reinterpret_cast<const uint32_t*>(&v2);
             }
-            *reinterpret_cast<uint4*>(yrow + c * 32 + u * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(yrow + col + u * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
         }
       }
@@ -400,7 +469,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
