@@ -10,7 +10,9 @@ from __future__ import annotations
 import ctypes
 import os
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libsokutou_b200.so")
+# SOKUTOU_B200_LIB overrides the in-tree library (e.g. a build with other compile-time tuning)
+LIB_PATH = os.environ.get("SOKUTOU_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib",
+                                                               "libsokutou_b200.so")
 
 SK_OK = 0
 ERRORS = {-1: "SK_ERR_INVALID_ARG", -2: "SK_ERR_UNSUPPORTED", -3: "SK_ERR_CUDA", -4: "SK_ERR_DEVICE",

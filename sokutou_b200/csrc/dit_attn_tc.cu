@@ -111,6 +111,42 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// 2^x for a pair, on the FMA/ALU pipes instead of the MUFU pipe: round-to-nearest range reduction
+// x = i + f, f in [-0.5, 0.5] (adding 1.5·2^23 leaves i in the low mantissa bits), 2^f by a degree-3
+// polynomial with p(0) = 1 fitted for this kernel by iteratively reweighted least squares on
+// Chebyshev points (max relative error 1.0e-4 in float32, far below the bf16 rounding of P), and i
+// added to the exponent field. Inputs are clamped at -127, which yields exactly 0 (masked keys).
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -127.f);
+  x.y = fmaxf(x.y, -127.f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 r = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(r, make_float2(-1.f, -1.f), x);
+  float2 q = __ffma2_rn(make_float2(0.05500892922282219f, 0.05500892922282219f), f,
+                        make_float2(0.2422109842300415f, 0.2422109842300415f));
+  q = __ffma2_rn(q, f, make_float2(0.6932829022407532f, 0.6932829022407532f));
+  q = __ffma2_rn(q, f, make_float2(1.f, 1.f));
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+// Exponent pairs per 8-key unit computed by ex2_poly2 instead of ex2.approx (MUFU), 0..4.
+// Measured on B200: 0 is fastest at these tile sizes (the softmax is not MUFU-bound).
+#ifndef SK_POLY_PAIRS
+#define SK_POLY_PAIRS 0
+#endif
+constexpr int kPolyPairs = SK_POLY_PAIRS;
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_commit_and_wait_read() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // Key bias of column `col` of key tile j in the log2 domain; -inf past the end of its segment.
 __device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloat16* bias, int b, int j, int n_lat,
                                            int col) {
@@ -130,7 +166,8 @@ template <int HD>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
-                   const __grid_constant__ CUtensorMap tmVc, const TcParams prm) {
+                   const __grid_constant__ CUtensorMap tmVc, const __grid_constant__ CUtensorMap tmY,
+                   const TcParams prm) {
   using Ly = TcLayout<HD>;
   constexpr int NSK = Ly::NSK, NSV = Ly::NSV;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -217,7 +254,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       uint32_t spins = 0;
       while (ok && (jk < ntiles || jv < ntiles)) {
         bool progress = false;
-        if (jk < ntiles && (jk < NSK || mbar_try_wait(&k_empty[jk % NSK], ((jk / NSK) - 1) & 1))) {
+        if (jk < ntiles && (jk < NSK || mbar_test(&k_empty[jk % NSK], ((jk / NSK) - 1) & 1))) {
           const int s = jk % NSK;
           uint8_t* dst = smem + Ly::OFF_K + s * Ly::KV_BYTES;
           mbar_arrive_expect_tx(&k_full[s], Ly::KV_BYTES);
@@ -232,7 +269,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           ++jk;
           progress = true;
         }
-        if (jv < ntiles && jv < jk && (jv < NSV || mbar_try_wait(&v_empty[jv % NSV], ((jv / NSV) - 1) & 1))) {
+        if (jv < ntiles && jv < jk && (jv < NSV || mbar_test(&v_empty[jv % NSV], ((jv / NSV) - 1) & 1))) {
           const int s = jv % NSV;
           uint8_t* dst = smem + Ly::OFF_V + s * Ly::KV_BYTES;
           mbar_arrive_expect_tx(&v_full[s], Ly::KV_BYTES);
@@ -280,14 +317,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tc_commit(&k_empty[s]);  // the K slot is free once this S is computed
         return true;
       };
-      if (ok) ok = issue_s(0);
-      if (ok && ntiles > 1) ok = issue_s(1);
-      for (int j = 0; j < ntiles && ok; ++j) {
+      // S_j needs K_j and its S buffer read (the softmax of tile j-2 has loaded it); PV_j needs P_j
+      // and V_j. Both are issued as soon as their inputs are ready, S first: a softmax warpgroup
+      // never waits for the P·V of its previous tile before its next S is there.
+      auto issue_pv = [&](int j) {
         const int sv = j % NSV, w = j & 1;
-        if (!mbar_wait(&p_full[w], (j >> 1) & 1, prm.err) || !mbar_wait(&v_full[sv], (j / NSV) & 1, prm.err)) {
-          ok = false;
-          break;
-        }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -297,7 +331,28 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         tc_commit(&o_done[w]);
         tc_commit(&v_empty[sv]);
-        if (j + 2 < ntiles) ok = issue_s(j + 2);
+      };
+      int js = 0, jp = 0;
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ok && jp < ntiles) {
+        bool progress = false;
+        if (js < ntiles && js < jp + 4 && mbar_test(&k_full[js % NSK], (js / NSK) & 1) &&
+            (js < 2 || mbar_test(&s_free[js & 1], ((js - 2) >> 1) & 1))) {
+          ok = issue_s(js);  // its waits are already satisfied
+          ++js;
+          progress = true;
+        }
+        if (ok && jp < js && mbar_test(&p_full[jp & 1], (jp >> 1) & 1) &&
+            mbar_test(&v_full[jp % NSV], (jp / NSV) & 1)) {
+          issue_pv(jp);
+          ++jp;
+          progress = true;
+        }
+        if (!progress && (++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
+          ok = false;
+        }
       }
       tc_commit(mma_done);
       mbar_wait(mma_done, 0, prm.err);
@@ -391,7 +446,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 dd = __fadd2_rn(make_float2(x[8 * u + 2 * e], x[8 * u + 2 * e + 1]), nm);
-          const float2 p = make_float2(ex2_approx(dd.x), ex2_approx(dd.y));
+          const float2 p = (e < kPolyPairs) ? ex2_poly2(dd) : make_float2(ex2_approx(dd.x), ex2_approx(dd.y));
           if (e & 1)
             ls1 = __fadd2_rn(ls1, p);
           else
@@ -434,9 +489,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const float l = a0 * l0 + a1 * l1;
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
       const float c0 = a0 * inv, c1 = a1 * inv;
-      const int qi = q0 + row;
-      __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(prm.y) + (((size_t)b * prm.L + qi) * prm.H + h) * HD;
-      constexpr int NC = HD / 64;  // 32-column chunks per warpgroup half
+      // y tile staged as 128B-swizzled [128 rows][64 cols] chunks over the (now free) P tiles, then
+      // written by TMA tensor stores; rows past L are clipped by the tensor map.
+      constexpr int NC = HD / 64;  // 32-column pieces per warpgroup half
       float o0[NC][32], o1[NC][32];
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
@@ -445,26 +500,35 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tmem_ld32(tO + HD + lane_off + col, o1[c]);
       }
       tmem_wait_ld();
-      if (qi < prm.L) {
 #pragma unroll
-        for (int c = 0; c < NC; ++c) {
-          const int col = wg * (HD / 2) + c * 32;
+      for (int c = 0; c < NC; ++c) {
+        const int col = wg * (HD / 2) + c * 32;  // first column of this piece
+        uint8_t* chunk = smem + Ly::OFF_P + (col >> 6) * (kBM * 128) + row * 128;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint32_t pk[4];
+        for (int u = 0; u < 4; ++u) {
+          uint32_t pk[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i0 = 8 * u + 2 * e;
-              // c1 == 0 when the second accumulator never ran: do not touch its contents
-              const float y0 = o0[c][i0] * c0 + (c1 != 0.f ? o1[c][i0] * c1 : 0.f);
-              const float y1 = o0[c][i0 + 1] * c0 + (c1 != 0.f ? o1[c][i0 + 1] * c1 : 0.f);
-              const __nv_bfloat162 v2 = __floats2bfloat162_rn(y0, y1);
-              pk[e] = *reinterpret_cast<const uint32_t*>(&v2);
-            }
-            *reinterpret_cast<uint4*>(yrow + col + u * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          for (int e = 0; e < 4; ++e) {
+            const int i0 = 8 * u + 2 * e;
+            // c1 == 0 when the second accumulator never ran: do not touch its contents
+            const float y0 = o0[c][i0] * c0 + (c1 != 0.f ? o1[c][i0] * c1 : 0.f);
+            const float y1 = o0[c][i0 + 1] * c0 + (c1 != 0.f ? o1[c][i0 + 1] * c1 : 0.f);
+            const __nv_bfloat162 v2 = __floats2bfloat162_rn(y0, y1);
+            pk[e] = *reinterpret_cast<const uint32_t*>(&v2);
           }
+          const int unit = ((col & 63) >> 3) + u;
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + ((unit ^ (row & 7)) << 4))),
+                       "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3])
+                       : "memory");
         }
       }
+      fence_proxy_async_smem();
+    }
+    named_bar_sync(3, 256);
+    if (okk && threadIdx.x == 0) {
+#pragma unroll
+      for (int c = 0; c < Ly::NCH; ++c) tma_store_4d(&tmY, smem + Ly::OFF_P + c * (kBM * 128), c * 64, h, q0, b);
+      tma_store_commit_and_wait_read();
     }
   }
   tc_fence_before();
@@ -536,6 +600,14 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     mkc = mq;  // never read: no conditioning key tiles
     mvc = mq;
   }
+  CUtensorMap my;
+  {
+    // y (B, L, H, hd): a box of 128 query rows of one head, 64 columns wide
+    cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)L, (cuuint64_t)B};
+    cuuint64_t str[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2, (cuuint64_t)L * H * HD * 2};
+    cuuint32_t box[4] = {64, 1, kBM, 1};
+    if (!make_map(&my, prm.y, 4, dims, str, box)) return SK_ERR_CUDA;
+  }
   const int smem = Ly::SMEM_ALLOC;
   static bool attr_done[64] = {};
   int dev = 0;
@@ -555,7 +627,7 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<HD>, mq, mk, mv, mkc, mvc, prm) != cudaSuccess) return SK_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<HD>, mq, mk, mv, mkc, mvc, my, prm) != cudaSuccess) return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }
 
