@@ -126,7 +126,7 @@ class ClockSampler:
 
     def __enter__(self):
         try:
-            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "25"]
             if self.uuid:
                 cmd += ["-i", self.uuid]
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)

@@ -105,6 +105,7 @@ SK_API int sk_dit_attention(const void* q, const void* k_lat, const void* v_lat,
  *   qk_w  : fp32 (2, H, hd) — q_norm then k_norm weights
  *   freqs : fp32 (>= L, hd/2, 2) — (cos, sin) per latent position
  *   q     : (B, H, L, hd);  k_lat, v_lat : (B, H, L, hd)   (dtype `dtype`)
+ *   hd    : 64 or 128; all buffers 16-byte aligned.
  */
 SK_API int sk_dit_qkv_prologue(const void* o4, const float* qk_w, const float* freqs,
                         void* q, void* k_lat, void* v_lat,

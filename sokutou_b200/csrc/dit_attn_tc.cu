@@ -439,14 +439,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       const float2 nm = make_float2(-m_use, -m_use);
+      // pass 1: all 128 exponentials in place (independent, so the MUFU pipe stays fed)
+#pragma unroll
+      for (int c = 0; c < kBN; c += 8) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 dd = __fadd2_rn(make_float2(x[c + 2 * e], x[c + 2 * e + 1]), nm);
+          const float2 p = (e < kPolyPairs) ? ex2_poly2(dd) : make_float2(ex2_approx(dd.x), ex2_approx(dd.y));
+          x[c + 2 * e] = p.x;
+          x[c + 2 * e + 1] = p.y;
+        }
+      }
+      // pass 2: row sum (two chains), bf16 packing, 16-byte swizzled stores of the P row
       float2 ls0 = make_float2(0.f, 0.f), ls1 = ls0;
 #pragma unroll
-      for (int u = 0; u < kBN / 8; ++u) {  // 16 units of 8 keys = 16 bytes
+      for (int u = 0; u < kBN / 8; ++u) {
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 dd = __fadd2_rn(make_float2(x[8 * u + 2 * e], x[8 * u + 2 * e + 1]), nm);
-          const float2 p = (e < kPolyPairs) ? ex2_poly2(dd) : make_float2(ex2_approx(dd.x), ex2_approx(dd.y));
+          const float2 p = make_float2(x[8 * u + 2 * e], x[8 * u + 2 * e + 1]);
           if (e & 1)
             ls1 = __fadd2_rn(ls1, p);
           else
@@ -455,10 +466,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           pk[e] = *reinterpret_cast<const uint32_t*>(&pb2);
         }
         const int chunk = u >> 3, unit = u & 7;
-        uint8_t* dst = prow + chunk * (kBM * 128) + ((unit ^ (row & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)), "r"(pk[0]), "r"(pk[1]),
-                     "r"(pk[2]), "r"(pk[3])
-                     : "memory");
+        *reinterpret_cast<uint4*>(prow + chunk * (kBM * 128) + ((unit ^ (row & 7)) << 4)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l_run += (ls0.x + ls0.y) + (ls1.x + ls1.y);
       fence_proxy_async_smem();
