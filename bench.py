@@ -423,6 +423,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-serving", action="store_true")
     ap.add_argument("--only-c1", action="store_true", help="headline workload only (for launch-list captures)")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU time budget of the reference arm")
     a = ap.parse_args()
     if a.impl == "reference":
         return reference_arm(a)
@@ -544,7 +545,7 @@ def reference_arm(a):
         return
     from sokutou_b200 import workloads as W
     shapes = [W.c1(L) for L in W.C1_SWEEP]
-    per_step = max(4.0, 20.0 / max(a.steps + a.warmup, 1))
+    per_step = max(min(4.0, a.cpu_seconds), a.cpu_seconds / max(a.steps + a.warmup, 1))
     for _ in range(a.warmup):
         cpu_dit_sample(shapes, seconds=per_step / 2)
     vals = []

@@ -20,7 +20,6 @@ from __future__ import annotations
 
 import multiprocessing as mp
 import os
-import queue
 import time
 from dataclasses import dataclass
 
@@ -71,80 +70,96 @@ def run_sharded(reqs: list[Request], executor, rank: int, world: int) -> list[tu
 
 # ---- host queue with worker processes ---------------------------------------------------------------
 
-def _worker(wid: int, device_env: str | None, make_executor, tasks, results):
+def _worker(wid: int, device_env: str | None, make_executor, conn):
     if device_env is not None:
         os.environ["CUDA_VISIBLE_DEVICES"] = device_env
     ex = make_executor(wid)
     while True:
-        r = tasks.get()
+        r = conn.recv()
         if r is None:
-            results.put(("exit", wid, None, 0.0))
             return
-        results.put(("claim", wid, r.rid, 0.0))
         t0 = time.perf_counter()
         ex.run(r)
-        results.put(("done", wid, r.rid, time.perf_counter() - t0))
+        conn.send((r.rid, time.perf_counter() - t0))
 
 
 def serve_local(reqs: list[Request], n_workers: int, make_executor, devices: list[str] | None = None,
                 timeout_s: float = 600.0) -> dict:
     """Run every request once on `n_workers` spawned worker processes fed from one host queue.
 
-    make_executor(worker_id) builds the worker's executor inside the worker (picklable callable).
-    devices[i] is written to CUDA_VISIBLE_DEVICES of worker i. A worker that dies has its claimed,
-    unfinished requests re-queued. Returns {"done": {rid: (worker, seconds)}, "requeued": [...],
-    "dead": [...], "wall_s": ...}.
+    The coordinator hands each idle worker the next request (longest first) over that worker's own pipe,
+    so it always knows what every worker holds. make_executor(worker_id) builds the worker's executor
+    inside the worker (a picklable callable); devices[i] becomes worker i's CUDA_VISIBLE_DEVICES. When
+    a worker process dies, the request it held goes back to the front of the queue for the survivors.
+    Returns {"done": {rid: (worker, seconds)}, "requeued": [...], "dead": [...], "wall_s": ...}.
     """
+    from collections import deque
+    from multiprocessing.connection import wait
+
     ctx = mp.get_context("spawn")
-    tasks, results = ctx.Queue(), ctx.Queue()
-    by_id = {r.rid: r for r in reqs}
-    for r in sorted(reqs, key=lambda r: (-cost_estimate(r), r.rid)):
-        tasks.put(r)
-    procs = {}
+    pending = deque(sorted(reqs, key=lambda r: (-cost_estimate(r), r.rid)))
+    procs, conns, inflight = {}, {}, {}
     for w in range(n_workers):
+        parent, child = ctx.Pipe()
         env = devices[w] if devices else None
-        p = ctx.Process(target=_worker, args=(w, env, make_executor, tasks, results), daemon=True)
+        p = ctx.Process(target=_worker, args=(w, env, make_executor, child), daemon=True)
         p.start()
-        procs[w] = p
-    claimed: dict[int, set[int]] = {w: set() for w in procs}
+        child.close()
+        procs[w], conns[w], inflight[w] = p, parent, None
+
+    def dispatch(w):
+        # an idle worker keeps waiting (no stop message yet): it may still take a re-queued request
+        inflight[w] = None
+        if pending:
+            r = pending.popleft()
+            inflight[w] = r
+            conns[w].send(r)
+
     done: dict[int, tuple[int, float]] = {}
     requeued, dead = [], []
     t0 = time.perf_counter()
     alive = set(procs)
-    sent_stop = False
-    while alive:
+    for w in list(alive):
+        dispatch(w)
+    while len(done) < len(reqs):
         if time.perf_counter() - t0 > timeout_s:
             for w in alive:
                 procs[w].kill()
             raise TimeoutError("serving did not finish")
-        try:
-            kind, w, rid, sec = results.get(timeout=0.2)
-            if kind == "claim":
-                claimed[w].add(rid)
-            elif kind == "done":
-                claimed[w].discard(rid)
+        if not alive:
+            raise RuntimeError(f"all workers died with {len(reqs) - len(done)} requests left")
+        handles = {conns[w]: ("msg", w) for w in alive}
+        handles.update({procs[w].sentinel: ("exit", w) for w in alive})
+        for h in wait(list(handles), timeout=0.5):
+            kind, w = handles[h]
+            if w not in alive:
+                continue
+            if kind == "msg":
+                try:
+                    rid, sec = conns[w].recv()
+                except (EOFError, OSError):
+                    continue  # the process is exiting; its sentinel reports it
                 done[rid] = (w, sec)
-            elif kind == "exit":
-                alive.discard(w)
-        except queue.Empty:
-            pass
-        for w in list(alive):
-            if not procs[w].is_alive() and procs[w].exitcode not in (None, 0):
+                dispatch(w)
+            elif not procs[w].is_alive():  # gone before being told to stop: dead
                 alive.discard(w)
                 dead.append(w)
-                for rid in sorted(claimed[w]):
-                    if rid not in done:
-                        requeued.append(rid)
-                        tasks.put(by_id[rid])
-                claimed[w].clear()
-        if len(done) == len(reqs) and not sent_stop:
-            for _ in range(n_workers):
-                tasks.put(None)
-            sent_stop = True
-        if not alive and len(done) < len(reqs):
-            raise RuntimeError(f"all workers died with {len(reqs) - len(done)} requests left")
+                r = inflight[w]
+                if r is not None and r.rid not in done:
+                    requeued.append(r.rid)
+                    pending.appendleft(r)
+                    idle = [v for v in alive if inflight[v] is None]
+                    if idle:
+                        dispatch(idle[0])
+    for w in alive:
+        try:
+            conns[w].send(None)
+        except (BrokenPipeError, OSError):
+            pass
     for p in procs.values():
         p.join(timeout=5)
+        if p.is_alive():
+            p.kill()
     return {"done": done, "requeued": requeued, "dead": dead, "wall_s": time.perf_counter() - t0}
 
 
