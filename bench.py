@@ -108,64 +108,103 @@ class Dist:
 
 # ---------------------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of this GPU's clocks and throttle reasons while the timed region runs."""
+    """This GPU's SM clock and clock-event reasons, read through NVML every `period_s` on a host
+    thread (nvidia-smi -lms as a fallback), and summarised over the timed window only: the code
+    being timed calls `window(True)` right before its first timed launch and `window(False)` after
+    the final synchronize. Reading only; no GPU setting is changed."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
-    def __init__(self, device: torch.device):
+    def __init__(self, device: torch.device, period_s: float = 0.002):
         self.uuid = None
         try:
-            u = torch.cuda.get_device_properties(device).uuid
-            self.uuid = "GPU-" + str(u)
+            self.uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
         except Exception:
             pass
+        self.period = period_s
+        self.samples: list[tuple[float, float, int]] = []  # (host time, sm MHz, reason bits)
+        self.windows: list[tuple[float, float]] = []
+        self._open = None
+        self.max_mhz = None
+        self.source = None
+        self._stop = threading.Event()
         self.proc = None
-        self.lines: list[str] = []
 
     def __enter__(self):
         try:
-            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "25"]
+            import pynvml
+            pynvml.nvmlInit()
+            h = (pynvml.nvmlDeviceGetHandleByUUID(self.uuid) if self.uuid else pynvml.nvmlDeviceGetHandleByIndex(0))
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.source = "nvml"
+            started = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((time.perf_counter(), float(mhz), int(bits)))
+                    except Exception:
+                        pass
+                    started.set()
+                    time.sleep(self.period)
+
+            self.th = threading.Thread(target=run, daemon=True)
+            self.th.start()
+            started.wait(timeout=2)
+        except Exception:
+            self._nvidia_smi()
+        return self
+
+    def _nvidia_smi(self):
+        try:
+            cmd = ["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                   "--format=csv,noheader,nounits", "-lms", "25"]
             if self.uuid:
                 cmd += ["-i", self.uuid]
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.th = threading.Thread(target=self._read, daemon=True)
-            self.th.start()
-        except Exception:
-            self.proc = None
-        return self
+            self.source = "nvidia-smi"
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            def read():
+                for line in self.proc.stdout:
+                    parts = [x.strip() for x in line.split(",")]
+                    try:
+                        self.max_mhz = float(parts[1])
+                        self.samples.append((time.perf_counter(), float(parts[0]), int(parts[2], 16)))
+                    except (ValueError, IndexError):
+                        continue
+
+            self.th = threading.Thread(target=read, daemon=True)
+            self.th.start()
+            time.sleep(0.5)  # nvidia-smi start-up
+        except Exception:
+            self.source = None
+
+    def window(self, start: bool):
+        if start:
+            self._open = time.perf_counter()
+        elif self._open is not None:
+            self.windows.append((self._open, time.perf_counter()))
+            self._open = None
 
     def __exit__(self, *a):
+        self._stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if getattr(self, "th", None):
             self.th.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[3:7]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = [x for x in self.samples if any(t0 <= x[0] <= t1 for t0, t1 in self.windows)]
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(x[2] & bit for x in inside))
+        return {"sm_mhz": statistics.median(x[1] for x in inside) if inside else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(inside), "source": self.source,
+                "window_ms": round(sum(t1 - t0 for t0, t1 in self.windows) * 1e3, 2)}
 
 
 # ---------------------------------------------------------------------------------------------- DiT
@@ -227,8 +266,10 @@ class DitSynthesis:
         return h2d, d2h
 
 
-def time_graphs(graphs, steps: int, warmup: int, dist: Dist):
-    """Device time (ms) of `steps` replays of all graphs, after `warmup`; max over ranks."""
+def time_graphs(graphs, steps: int, warmup: int, dist: Dist, label: str = "timed", clk=None):
+    """Device time (ms) of `steps` replays of all graphs, after `warmup`; max over ranks. The timed
+    replays sit in an NVTX range named `label`, so a profiler can select exactly them
+    (ncu --nvtx --nvtx-include "<label>/")."""
     for _ in range(warmup):
         for g in graphs:
             g.replay()
@@ -236,12 +277,18 @@ def time_graphs(graphs, steps: int, warmup: int, dist: Dist):
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clk is not None:
+        clk.window(True)
+    torch.cuda.nvtx.range_push(label)
     e0.record()
     for _ in range(steps):
         for g in graphs:
             g.replay()
     e1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
+    if clk is not None:
+        clk.window(False)
     dist.barrier()
     torch.cuda.synchronize()
     return dist.max(e0.elapsed_time(e1))
@@ -446,7 +493,7 @@ def main():
     flops_step = sum(s.flops for s in syn)
     launches_step = sum(len(s.calls) for s in syn)
     with ClockSampler(dev) as clk:
-        ms = time_graphs([s.graph for s in syn], a.steps, max(a.warmup, 3), dist)
+        ms = time_graphs([s.graph for s in syn], a.steps, max(a.warmup, 3), dist, label="c1_step", clk=clk)
     ms_step = ms / a.steps
     value = dist.sum(flops_step) / (ms_step / 1e3) / 1e12
     per_gpu = flops_step / (ms_step / 1e3) / 1e12
