@@ -437,6 +437,51 @@ def cpu_dit_sample(shapes, seconds: float = 12.0, threads: int | None = None):
         f"timed ~{seconds:.0f}s total, scaled to the synthesis call mix"
 
 
+# ------------------------------------------------------------------------------- fused attention block
+def layer_block(device, dist: Dist, calls: int = 120, sets: int = 4) -> dict:
+    """One DiT layer's attention block — Q/K/V producer, attention, gate (engine/fused.py:293-298) — as
+    one fused launch and as the three separate launches, each timed over `calls` graph-replayed calls
+    rotating `sets` input sets (o4 and ctx K/V distinct per set). Reports microseconds per block."""
+    from sokutou_b200 import dit, workloads as W
+    out = {}
+    for name, shape, B in (("c1_L512_b3", W.c1(512), 3), ("c1_L128_b1", W.c1(128), 1), ("c2_b3", W.C2, 3)):
+        g = torch.Generator(device=device).manual_seed(5)
+        H, hd, L, S = shape.H, shape.hd, shape.L, shape.S
+        qk_w = W.dit_qk_weights(shape, device)
+        freqs = W.dit_freqs(L, hd, device=device)
+        bias = dit.cfg_bias(L, shape.Tb, shape.Sp, L, 40, device=device)[:B].contiguous()
+        ins = []
+        for _ in range(sets):
+            o4 = (torch.randn(B * L, 4 * H * hd, device=device, generator=g) * shape.sigma).bfloat16()
+            kc = torch.randn(S, H, hd, device=device, generator=g)
+            kc = (kc * torch.rsqrt(kc.pow(2).mean(-1, keepdim=True))).bfloat16()
+            vc = (torch.randn(S, H, hd, device=device, generator=g) * shape.sigma).bfloat16()
+            ins.append((o4, kc, vc))
+        res = {}
+        for mode in ("fused", "separate"):
+            layers = [dit.DitLayerAttention(B, L, H, hd, S, torch.bfloat16, device, fused=(mode == "fused"))
+                      for _ in range(sets)]
+            run = lambda: [layers[i % sets](ins[i % sets][0], qk_w, freqs, ins[i % sets][1], ins[i % sets][2], bias)
+                           for i in range(calls)]
+            st = torch.cuda.Stream(device)
+            st.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(st):
+                run()
+            torch.cuda.current_stream(device).wait_stream(st)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                run()
+            ms = time_graphs([gr], 3, 3, dist)
+            res[f"{mode}_us"] = round(ms * 1e3 / (3 * calls), 3)
+            del gr
+        res["flops_per_block"] = shape.flops(B)
+        res["fused_tflops"] = round(shape.flops(B) / (res["fused_us"] * 1e-6) / 1e12, 2)
+        res["speedup"] = round(res["separate_us"] / res["fused_us"], 3)
+        out[name] = res
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------------------------- serving
 def serving(dist: Dist, device):
     """64 requests, longest-first static sharding over the ranks; sentences/s."""
@@ -548,6 +593,9 @@ def main():
     del dec
     torch.cuda.empty_cache()
 
+    # ---- fused attention block vs its three launches
+    blocks = layer_block(dev, dist)
+
     # ---- c4 serving
     serv = None if a.no_serving else serving(dist, dev)
     err = ops.device_error()
@@ -578,7 +626,7 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": UNIT,
                          "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} bf16 burst",
                          "frac_of_spec": round(achieved / SPEC["bf16_tflops"], 4), "traffic": traffic},
-            "c2": c2_res, "c3": c3_res, "serving": serv, "cpu_baseline": cpu,
+            "c2": c2_res, "c3": c3_res, "layer_block": blocks, "serving": serv, "cpu_baseline": cpu,
             "clocks": clk.summary(), "device_error": err,
         }
         print(json.dumps(line), flush=True)

@@ -55,6 +55,7 @@ extern "C" {
 /* ---- dtypes ---------------------------------------------------------------------------------- */
 #define SK_BF16 0
 #define SK_F32 1
+#define SK_E4M3 2   /* FP8 e4m3 output (sk_dit_gate only) */
 
 /* Library version (major*10000 + minor*100 + patch). */
 SK_API int sk_version(void);
@@ -110,6 +111,52 @@ SK_API int sk_dit_attention(const void* q, const void* k_lat, const void* v_lat,
 SK_API int sk_dit_qkv_prologue(const void* o4, const float* qk_w, const float* freqs,
                         void* q, void* k_lat, void* v_lat,
                         int B, int L, int H, int hd, float eps, int dtype, void* stream);
+
+/*
+ * The whole attention block of one DiT layer (bf16): the Q/K/V producer, the attention and the gate
+ * consumer, replacing the three launches at engine/fused.py:293-298 — `qkv` (engine/fused.py:117-180),
+ * F.scaled_dot_product_attention (:295) and `gate` (:182-190). At hd = 64 it takes two launches: the
+ * producer writes only q and k, and the attention kernel reads v and the gate tile straight from o4
+ * and writes the gated output (neither v nor y reaches HBM). At hd = 128 it runs the three kernels
+ * (y through `out`, gated in place), which measured faster there. Each launch's set-up overlaps the
+ * previous kernel through programmatic dependent launch:
+ *
+ *   q, k  = per-head RMSNorm (× qk_w) + RoPE (heads h < H/2) of the q/k quarters of o4
+ *   y     = softmax(q·kᵀ·scale + key_bias) · v over keys [latent (L) | ctx (S)], rounded to bf16
+ *   out   = y · sigmoid(o4[:, 3D:4D]) in fp32, rounded to bf16
+ *
+ *   o4           : (B*L, 4*H*hd) bf16 rows [q | k | v | gate]
+ *   qk_w, freqs  : fp32 (2, H, hd) and (>= L, hd/2, 2), as for sk_dit_qkv_prologue
+ *   k_ctx, v_ctx, key_bias, ctx_batch_stride, bias_batch_stride, scale: as for sk_dit_attention
+ *   out          : (B, L, H, hd) = (B*L, H*hd) bf16
+ *   q_buf, k_buf, v_buf : caller-owned scratch, (B, H, L, hd) bf16 each, overwritten (v_buf is left
+ *                  untouched at hd = 64); the engine already allocates its q/k/v buffers before
+ *                  capture (engine/fused.py:277-282). out must not overlap o4.
+ *   dtype        : SK_BF16 only (the fp32 parity mode runs the three separate entry points)
+ *   hd 64 or 128, H even, all pointers 16-byte aligned.
+ * Same bits as sk_dit_qkv_prologue + sk_dit_attention + sk_dit_gate on the same inputs.
+ */
+SK_API int sk_dit_attention_layer(const void* o4, const float* qk_w, const float* freqs,
+                                  const void* k_ctx, const void* v_ctx, const void* key_bias, void* out,
+                                  void* q_buf, void* k_buf, void* v_buf, int B, int H, int L, int S, int hd,
+                                  long long ctx_batch_stride, long long bias_batch_stride,
+                                  float eps, int dtype, float scale, void* stream);
+
+/*
+ * The attention consumer of one DiT layer: out[r, c] = y[r, c] · sigmoid(o4[r, 3·D + c]) for every
+ * row r of the B·L latent rows and c < D = H·hd. Replaces the `gate` kernel, engine/fused.py:182-190
+ * (launch :296-298): fp32 product y · (1 / (1 + expf(-g))), rounded once to the output type.
+ *
+ *   y         : (rows, D) = the (B, L, H, hd) output of sk_dit_attention, dtype `dtype`
+ *   o4        : (rows, 4·D) fused projection rows [q | k | v | gate], dtype `dtype`
+ *   out       : (rows, D) in `out_dtype`: the same dtype, or SK_E4M3 — FP8 e4m3 of value·out_scale,
+ *               round to nearest even, ±448 saturation, NaN → 0x7f (the reference's FP8 GEMM input,
+ *               engine/fused.py:52-76, engine/fp8.py)
+ *   D         : multiple of 8; y and o4 16-byte aligned, out 16-byte (8-byte for SK_E4M3) aligned.
+ *               out may be y itself (same dtype): the gate is then applied in place.
+ */
+SK_API int sk_dit_gate(const void* y, const void* o4, void* out, long long rows, int D, int dtype,
+                       int out_dtype, float out_scale, void* stream);
 
 /* ---- 2. Qwen3 talker decode attention --------------------------------------------------------- */
 

@@ -7,7 +7,9 @@ Restates, in numpy float64:
   - the CFG key mask (engine/bucket.py:252-258) and its additive form (engine/fused.py:373-378);
   - the attention itself, F.scaled_dot_product_attention(q, k, v, attn_mask=bias)
     (engine/fused.py:295): softmax(q·kᵀ/sqrt(hd) + bias)·v, non-causal, keys ordered
-    [latent | text | speaker] (engine/fast.py:167-168).
+    [latent | text | speaker] (engine/fast.py:167-168);
+  - the consumer `gate` (engine/fused.py:182-190): y · sigmoid(gate) in float32, rounded once, with
+    the FP8 e4m3 output form (engine/fused.py:52-76).
 
 The RoPE frequency table of Irodori-TTS (`model._rope_freqs`, engine/fast.py:264) lives in the
 third-party package irodori_tts @ 7ed4374 (not present here); `rope_freqs` restates the
@@ -145,3 +147,74 @@ def dit_attention_torch_cpu(q, k_lat, v_lat, k_ctx, v_ctx, bias, threads: int | 
     v = torch.cat([v_lat, v_ctx.expand(B, -1, -1, -1).transpose(1, 2)], dim=2)
     y = F.scaled_dot_product_attention(q, k, v, attn_mask=bias.reshape(-1, 1, 1, k.shape[2]))
     return y.transpose(1, 2)
+
+
+# ---- attention consumer: gate ------------------------------------------------------------------------
+
+def _e4m3_table() -> np.ndarray:
+    """Values of the 127 non-negative finite e4m3 codes 0x00..0x7e (bias 7, 3 mantissa bits,
+    subnormal step 2^-9), indexed by code."""
+    codes = np.arange(0x7F)
+    e, m = codes >> 3, codes & 7
+    return np.where(e == 0, m * 2.0 ** -9, (1 + m / 8.0) * 2.0 ** (e - 7.0))
+
+
+def e4m3_encode(x) -> np.ndarray:
+    """float32 -> e4m3 code (uint8) as the reference's FP8 writer defines it (engine/fused.py:60-72):
+    nearest representable value with ties to the even code, magnitudes at or past 448 -> ±448 (0x7e),
+    NaN -> 0x7f, sign kept (also for zero). Written as a nearest-neighbour search over the code
+    table rather than bit arithmetic."""
+    f = np.asarray(x, dtype=np.float32)
+    a = np.abs(f).astype(np.float64)
+    sign = (f.view(np.uint32) >> 24).astype(np.uint8) & 0x80
+    tab = _e4m3_table()
+    a_c = np.minimum(np.nan_to_num(a, nan=0.0, posinf=448.0), 448.0)
+    hi = np.clip(np.searchsorted(tab, a_c, side="left"), 0, len(tab) - 1)   # first value >= a
+    lo = np.clip(hi - 1, 0, len(tab) - 1)
+    d_hi, d_lo = tab[hi] - a_c, a_c - tab[lo]
+    pick_hi = (d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo).astype(np.uint8)
+    code = np.where(a_c >= 448.0, 0x7E, code).astype(np.uint8)
+    out = (code | sign).astype(np.uint8)
+    return np.where(np.isnan(f), np.uint8(0x7F), out).astype(np.uint8)
+
+
+def e4m3_decode(c) -> np.ndarray:
+    c = np.asarray(c, dtype=np.uint8)
+    mag = _e4m3_table()[np.minimum(c & 0x7F, 0x7E)]
+    mag = np.where((c & 0x7F) == 0x7F, np.nan, mag)
+    return np.where(c & 0x80, -mag, mag).astype(np.float32)
+
+
+def gate(y, o4, out: str = "f32", out_scale: float = 1.0) -> np.ndarray:
+    """out[r, c] = y[r, c] · (1 / (1 + exp(-o4[r, 3D + c]))) in float32 (engine/fused.py:182-190),
+    then rounded once: out = "f32" (as is), "bf16" (round to nearest even, returned as float32) or
+    "e4m3" (codes of value · out_scale). y: (rows, D) or anything holding rows·D values."""
+    o4 = np.asarray(o4, dtype=np.float32)
+    rows, D = o4.shape[0], o4.shape[1] // 4
+    yv = np.asarray(y, dtype=np.float32).reshape(rows, D)
+    g = o4[:, 3 * D:]
+    with np.errstate(over="ignore"):
+        sig = np.float32(1.0) / (np.float32(1.0) + np.exp(-g, dtype=np.float32))
+    r = (yv * sig).astype(np.float32)
+    if out == "f32":
+        return r
+    if out == "bf16":
+        return bf16_round(r)
+    if out == "e4m3":
+        return e4m3_encode((r * np.float32(out_scale)).astype(np.float32))
+    raise ValueError(out)
+
+
+def attention_layer(o4, qk_w, freqs, B: int, L: int, H: int, hd: int, eps: float, k_ctx=None, v_ctx=None,
+                    bias=None, bf16: bool = True) -> np.ndarray:
+    """The attention block of one DiT layer as the engine runs it (engine/fused.py:293-298): the `qkv`
+    producer, SDPA over [latent | ctx] keys, the `gate` consumer. With bf16, q/k/v and the SDPA output
+    are rounded to bfloat16 between the steps as the engine's buffers hold them, and the gated product
+    is rounded once. Returns (B*L, H*hd) as float32."""
+    q, k, v = qkv_prologue(o4, qk_w, freqs, B, L, H, hd, eps, bf16)
+    y = dit_attention(q, k, v, k_ctx, v_ctx, bias)
+    y = y.reshape(B * L, H * hd).astype(np.float32)
+    if bf16:
+        y = bf16_round(y)
+    return gate(y, o4, "bf16" if bf16 else "f32")

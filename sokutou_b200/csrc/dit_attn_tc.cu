@@ -73,8 +73,9 @@ struct TcLayout {
   // for the (max, sum) of its kBM rows that the epilogue exchanges
   static constexpr int OFF_BIAS = OFF_P + 2 * P_BYTES;
   static constexpr int OFF_BAR = OFF_BIAS + 4 * kBN * 4;
-  // q_full, k_full/k_empty[NSK], v_full/v_empty[NSV], s_full[2], s_free[2], p_full[2], o_done[2], mma_done
-  static constexpr int NBAR = 1 + 2 * NSK + 2 * NSV + 8 + 1;
+  // q_full, k_full/k_empty[NSK], v_full/v_empty[NSV], s_full[2], s_free[2], p_full[2], o_done[2], mma_done,
+  // and for the fused block: q_free, gate_full
+  static constexpr int NBAR = 1 + 2 * NSK + 2 * NSV + 8 + 1 + 2;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_TMEM + 16;
   // The dynamic shared-memory base is 1024-byte aligned on sm_100 (checked at run time); the
@@ -92,6 +93,7 @@ struct TcParams {
   float scale_log2;      // softmax scale * log2(e)
   int ctx_batched;       // 1: ctx map has a batch coordinate
   int* err;
+  int D;                 // H * hd (fused block: v and gate column offsets in o4)
 };
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -145,6 +147,12 @@ constexpr int kPolyPairs = SK_POLY_PAIRS;
 #define SK_K_LEAD 0
 #endif
 constexpr int kKLead = SK_K_LEAD;
+// Key tiles from this index on are prefetched into L2 (K and V, in the order they are needed) right
+// after Q is requested, so that their ring loads later hit L2 instead of waiting on DRAM; 0 = off.
+#ifndef SK_L2_PREFETCH_FROM
+#define SK_L2_PREFETCH_FROM 0
+#endif
+constexpr int kL2PrefetchFrom = SK_L2_PREFETCH_FROM;
 // Back-off (ns) of the polling producer and MMA threads after a pass that found nothing to issue;
 // their spins share issue slots with the softmax warps of the same sub-partition.
 #ifndef SK_PRODUCER_SLEEP_NS
@@ -180,11 +188,16 @@ __device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloa
   return bias ? __bfloat162float(bias[(size_t)b * prm.bias_bs + key]) * kLog2e : 0.f;
 }
 
-template <int HD>
+// FUSED = false: attention over q (B, H, L, hd), latent k/v (B, H, Lk, hd) and the ctx K/V, y (B, L, H, hd).
+// FUSED = true: the attention of a DiT layer's fused block — the epilogue reads the gate tile from the
+// projection rows o4 (B·L, 4·D) through tmG and writes y · sigmoid(gate). VO4 = true: the latent v
+// tiles also come straight from o4 (tmV over o4) instead of the producer's (B, H, L, hd) buffer.
+template <int HD, bool FUSED, bool VO4>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
                    const __grid_constant__ CUtensorMap tmVc, const __grid_constant__ CUtensorMap tmY,
+                   const __grid_constant__ CUtensorMap tmG,
                    const TcParams prm) {
   using Ly = TcLayout<HD>;
   constexpr int NSK = Ly::NSK, NSV = Ly::NSV;
@@ -206,6 +219,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* p_full = s_free + 2;
   uint64_t* o_done = p_full + 2;
   uint64_t* mma_done = o_done + 2;
+  uint64_t* q_free = mma_done + 1;     // fused: every S = Q·Kᵀ done, the Q area may take the gate tile
+  uint64_t* gate_full = q_free + 1;    // fused: gate tile landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::OFF_TMEM);
   float* bias_s = reinterpret_cast<float*>(smem + Ly::OFF_BIAS);
 
@@ -231,12 +246,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(&o_done[i], 1);
     }
     mbar_init(mma_done, 1);
+    if (FUSED) {
+      mbar_init(q_free, 1);
+      mbar_init(gate_full, 1);
+    }
     fence_mbar_init();
   }
   if (warp == kWarpProducer && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    if (FUSED) tma_prefetch_desc(&tmG);
     if (n_ctx) {
       tma_prefetch_desc(&tmKc);
       tma_prefetch_desc(&tmVc);
@@ -260,12 +280,33 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   if (warp == kWarpProducer) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const int bh = b * prm.H + h;
       const int bc = prm.ctx_batched ? b : 0;
+      // latent tiles: (column, row, batch·head) of (B·H, L, hd) buffers; the fused block's v (and gate)
+      // tiles are (column, row, batch) of o4 at column offset 2·D (3·D) plus the head's h·hd
+      const int lz = b * prm.H + h, lzv = VO4 ? b : lz;
+      const int xv = VO4 ? 2 * prm.D + h * HD : 0;
       mbar_arrive_expect_tx(q_full, Ly::Q_BYTES);
 #pragma unroll
       for (int c = 0; c < Ly::NCH; ++c)
-        tma_load_3d(smem + Ly::OFF_Q + c * (kBM * 128), &tmQ, q_full, c * 64, q0, bh);
+        tma_load_3d(smem + Ly::OFF_Q + c * (kBM * 128), &tmQ, q_full, c * 64, q0, lz);
+      if (FUSED) {  // the gate tile is loaded after the last S = Q·Kᵀ; start its trip to L2 now
+#pragma unroll
+        for (int c = 0; c < Ly::NCH; ++c) tma_prefetch_l2_3d(&tmG, 3 * prm.D + h * HD + c * 64, q0, b);
+      }
+      if (kL2PrefetchFrom > 0) {
+        for (int j = kL2PrefetchFrom; j < ntiles; ++j) {
+#pragma unroll
+          for (int c = 0; c < Ly::NCH; ++c) {
+            if (j < n_lat) {
+              tma_prefetch_l2_3d(&tmK, c * 64, j * kBN, lz);
+              tma_prefetch_l2_3d(&tmV, xv + c * 64, j * kBN, lzv);
+            } else {
+              tma_prefetch_l2_4d(&tmKc, c * 64, h, (j - n_lat) * kBN, bc);
+              tma_prefetch_l2_4d(&tmVc, c * 64, h, (j - n_lat) * kBN, bc);
+            }
+          }
+        }
+      }
       int jk = 0, jv = 0;
       bool ok = true;
       const uint64_t t0 = globaltimer_ns();
@@ -278,7 +319,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           mbar_arrive_expect_tx(&k_full[s], Ly::KV_BYTES);
           if (jk < n_lat) {
 #pragma unroll
-            for (int c = 0; c < Ly::NCH; ++c) tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, jk * kBN, bh);
+            for (int c = 0; c < Ly::NCH; ++c)
+              tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, jk * kBN, lz);
           } else {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
@@ -294,7 +336,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           mbar_arrive_expect_tx(&v_full[s], Ly::KV_BYTES);
           if (jv < n_lat) {
 #pragma unroll
-            for (int c = 0; c < Ly::NCH; ++c) tma_load_3d(dst + c * (kBN * 128), &tmV, &v_full[s], c * 64, jv * kBN, bh);
+            for (int c = 0; c < Ly::NCH; ++c)
+              tma_load_3d(dst + c * (kBN * 128), &tmV, &v_full[s], xv + c * 64, jv * kBN, lzv);
           } else {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
@@ -311,8 +354,19 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
         }
       }
+      // fused: the gate tile goes where Q was, once no MMA reads Q any more (a blocking wait: the
+      // softmax warps sharing this sub-partition keep its issue slots)
+      bool gate_issued = false;
+      if (FUSED && ok && mbar_wait(q_free, 0, prm.err)) {
+        mbar_arrive_expect_tx(gate_full, Ly::Q_BYTES);
+#pragma unroll
+        for (int c = 0; c < Ly::NCH; ++c)
+          tma_load_3d(smem + Ly::OFF_Q + c * (kBM * 128), &tmG, gate_full, 3 * prm.D + h * HD + c * 64, q0, b);
+        gate_issued = true;
+      }
       // Keep shared memory alive until every copy issued has landed (already true on the normal path).
       mbar_wait(q_full, 0, prm.err);
+      if (FUSED && gate_issued) mbar_wait(gate_full, 0, prm.err);
       for (int j = (jk > NSK ? jk - NSK : 0); j < jk; ++j) mbar_wait(&k_full[j % NSK], (j / NSK) & 1, prm.err);
       for (int j = (jv > NSV ? jv - NSV : 0); j < jv; ++j) mbar_wait(&v_full[j % NSV], (j / NSV) & 1, prm.err);
     }
@@ -363,6 +417,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             (js < 2 || mbar_test(&s_free[js & 1], ((js - 2) >> 1) & 1))) {
           ok = issue_s(js);  // its waits are already satisfied
           ++js;
+          if (FUSED && js == ntiles) tc_commit(q_free);  // Q is read by no further MMA
           progress = true;
         }
         if (ok && jp < js && mbar_test(&p_full[jp & 1], (jp >> 1) & 1) &&
@@ -541,6 +596,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const int jl = ((ntiles - 1 - w) >> 1) * 2 + w;
       if (jl < ntiles && jl >= 0) okk = mbar_wait(&o_done[w], (jl >> 1) & 1, prm.err);
     }
+    if (FUSED && okk) okk = mbar_wait(gate_full, 0, prm.err);
     okk = __all_sync(0xffffffffu, okk);
     if (okk) {
       tc_fence_after();
@@ -570,16 +626,30 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint32_t pk[4];
+          const int unit = ((col & 63) >> 3) + u;
+          uint32_t gw[4] = {0, 0, 0, 0};
+          if (FUSED) {  // the gate tile sits where Q was, in the same swizzled layout
+            const uint4 g4 = *reinterpret_cast<const uint4*>(smem + Ly::OFF_Q + (col >> 6) * (kBM * 128) + row * 128 +
+                                                             ((unit ^ (row & 7)) << 4));
+            gw[0] = g4.x, gw[1] = g4.y, gw[2] = g4.z, gw[3] = g4.w;
+          }
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int i0 = 8 * u + 2 * e;
             // c1 == 0 when the second accumulator never ran: do not touch its contents
-            const float y0 = o0[c][i0] * c0 + (c1 != 0.f ? o1[c][i0] * c1 : 0.f);
-            const float y1 = o0[c][i0 + 1] * c0 + (c1 != 0.f ? o1[c][i0 + 1] * c1 : 0.f);
+            float y0 = o0[c][i0] * c0 + (c1 != 0.f ? o1[c][i0] * c1 : 0.f);
+            float y1 = o0[c][i0 + 1] * c0 + (c1 != 0.f ? o1[c][i0 + 1] * c1 : 0.f);
+            if (FUSED) {
+              // the attention output rounded to bf16 as SDPA returns it, then the `gate` arithmetic
+              // (engine/fused.py:182-190): y · (1 / (1 + expf(-g))) in fp32 (the reciprocal correctly
+              // rounded, as the IEEE division), rounded once
+              y0 = __bfloat162float(__float2bfloat16_rn(y0)) * __frcp_rn(1.0f + expf(-__uint_as_float(gw[e] << 16)));
+              y1 = __bfloat162float(__float2bfloat16_rn(y1)) *
+                   __frcp_rn(1.0f + expf(-__uint_as_float(gw[e] & 0xffff0000u)));
+            }
             const __nv_bfloat162 v2 = __floats2bfloat162_rn(y0, y1);
             pk[e] = *reinterpret_cast<const uint32_t*>(&v2);
           }
-          const int unit = ((col & 63) >> 3) + u;
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + ((unit ^ (row & 7)) << 4))),
                        "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3])
                        : "memory");
@@ -631,9 +701,11 @@ static bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int HD>
+// q (B, H, L, hd), k_lat (B, H, Lk, hd); v_lat (B, H, Lk, hd), or with VO4 the projection rows o4;
+// o4 (B·L, 4·D): the gate source of the fused block (unused otherwise).
+template <int HD, bool FUSED, bool VO4>
 static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const void* k_ctx, const void* v_ctx,
-                     long long ctx_bs, const TcParams& prm, int B, cudaStream_t st) {
+                     const void* o4, long long ctx_bs, const TcParams& prm, int B, cudaStream_t st) {
   using Ly = TcLayout<HD>;
   const int H = prm.H, L = prm.L, Lk = prm.Lk, S = prm.S;
   CUtensorMap mq, mk, mv, mkc, mvc;
@@ -647,7 +719,8 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)Lk, (cuuint64_t)B * H};
     cuuint64_t str[2] = {(cuuint64_t)HD * 2, (cuuint64_t)Lk * HD * 2};
     cuuint32_t box[3] = {64, kBN, 1};
-    if (!make_map(&mk, k_lat, 3, dims, str, box) || !make_map(&mv, v_lat, 3, dims, str, box)) return SK_ERR_CUDA;
+    if (!make_map(&mk, k_lat, 3, dims, str, box)) return SK_ERR_CUDA;
+    if (!VO4 && !make_map(&mv, v_lat, 3, dims, str, box)) return SK_ERR_CUDA;
   } else {
     mk = mq;  // never read: no latent key tiles
     mv = mq;
@@ -663,6 +736,16 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     mkc = mq;  // never read: no conditioning key tiles
     mvc = mq;
   }
+  CUtensorMap mg = mq;  // never read unless FUSED
+  if (FUSED || VO4) {
+    // o4 as (B, L, 4·D): v and gate tiles are boxes of 128 rows x 64 columns at column offsets
+    // 2·D + h·hd and 3·D + h·hd; rows past L read as zeros
+    cuuint64_t d4[3] = {(cuuint64_t)4 * prm.D, (cuuint64_t)L, (cuuint64_t)B};
+    cuuint64_t s4[2] = {(cuuint64_t)4 * prm.D * 2, (cuuint64_t)L * 4 * prm.D * 2};
+    cuuint32_t box[3] = {64, kBM, 1};
+    if (!make_map(&mg, o4, 3, d4, s4, box)) return SK_ERR_CUDA;
+    if (VO4) mv = mg;
+  }
   CUtensorMap my;
   {
     // y (B, L, H, hd): a box of 128 query rows of one head, 64 columns wide
@@ -676,7 +759,8 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_tc_kernel<HD, FUSED, VO4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
       return SK_ERR_CUDA;
     attr_done[dev] = true;
   }
@@ -689,8 +773,9 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // set-up overlaps the previous kernel
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<HD>, mq, mk, mv, mkc, mvc, my, prm) != cudaSuccess) return SK_ERR_CUDA;
+  cfg.numAttrs = sk::kUsePdl ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<HD, FUSED, VO4>, mq, mk, mv, mkc, mvc, my, mg, prm) != cudaSuccess)
+    return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }
 
@@ -732,7 +817,51 @@ extern "C" int sk_dit_attention(const void* q, const void* k_lat, const void* v_
                                        bias_batch_stride, sc, st);
   int* err = sk_error_word_ptr();
   if (!err) return SK_ERR_CUDA;
-  TcParams prm{key_bias, bias_batch_stride, y, H, L, Lk, S, sc * kLog2e, ctx_batch_stride != 0 ? 1 : 0, err};
-  return hd == 64 ? launch_tc<64>(q, k_lat, v_lat, k_ctx, v_ctx, ctx_batch_stride, prm, B, st)
-                  : launch_tc<128>(q, k_lat, v_lat, k_ctx, v_ctx, ctx_batch_stride, prm, B, st);
+  TcParams prm{key_bias, bias_batch_stride, y, H, L, Lk, S, sc * kLog2e, ctx_batch_stride != 0 ? 1 : 0, err, H * hd};
+  return hd == 64 ? launch_tc<64, false, false>(q, k_lat, v_lat, k_ctx, v_ctx, nullptr, ctx_batch_stride, prm, B, st)
+                  : launch_tc<128, false, false>(q, k_lat, v_lat, k_ctx, v_ctx, nullptr, ctx_batch_stride, prm, B, st);
+}
+
+int sk_launch_qkv_prologue(const void* o4, const float* qk_w, const float* freqs, void* q, void* k, void* v, int B,
+                           int L, int H, int hd, float eps, int dtype, cudaStream_t st);
+
+extern "C" int sk_dit_attention_layer(const void* o4, const float* qk_w, const float* freqs, const void* k_ctx,
+                                      const void* v_ctx, const void* key_bias, void* out, void* q_buf, void* k_buf,
+                                      void* v_buf, int B, int H, int L, int S, int hd, long long ctx_batch_stride,
+                                      long long bias_batch_stride, float eps, int dtype, float scale, void* stream) {
+  using namespace sk::dit;
+  if (!o4 || !qk_w || !freqs || !out || !q_buf || !k_buf || !v_buf) return SK_ERR_INVALID_ARG;
+  if (B <= 0 || H <= 0 || L <= 0 || S < 0 || H % 2) return SK_ERR_INVALID_ARG;
+  if (S > 0 && (!k_ctx || !v_ctx)) return SK_ERR_INVALID_ARG;
+  if (ctx_batch_stride < 0 || bias_batch_stride < 0) return SK_ERR_INVALID_ARG;
+  if (hd != 64 && hd != 128) return SK_ERR_UNSUPPORTED;
+  if (dtype != SK_BF16) return SK_ERR_UNSUPPORTED;  // the fp32 mode runs the three separate calls
+  const uintptr_t al = reinterpret_cast<uintptr_t>(o4) | reinterpret_cast<uintptr_t>(qk_w) |
+                       reinterpret_cast<uintptr_t>(freqs) | reinterpret_cast<uintptr_t>(k_ctx) |
+                       reinterpret_cast<uintptr_t>(v_ctx) | reinterpret_cast<uintptr_t>(out) |
+                       reinterpret_cast<uintptr_t>(q_buf) | reinterpret_cast<uintptr_t>(k_buf) |
+                       reinterpret_cast<uintptr_t>(v_buf);
+  if (al & 15) return SK_ERR_INVALID_ARG;
+  if (S > 0 && ctx_batch_stride != 0 && ((ctx_batch_stride * 2) & 15)) return SK_ERR_INVALID_ARG;
+  int rc = sk_check_device();
+  if (rc != SK_OK) return rc;
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)hd);
+  TcParams prm{key_bias, bias_batch_stride, out, H, L, L, S, sc * kLog2e, ctx_batch_stride != 0 ? 1 : 0, err, H * hd};
+  if (hd == 64) {
+    // two launches: q and k (normalised, rotated) into the caller's buffers; the attention reads v
+    // and the gate straight from o4 and writes y · sigmoid(gate)
+    rc = sk_launch_qkv_prologue(o4, qk_w, freqs, q_buf, k_buf, nullptr, B, L, H, hd, eps, SK_BF16, st);
+    if (rc != SK_OK) return rc;
+    return launch_tc<64, true, true>(q_buf, k_buf, o4, k_ctx, v_ctx, o4, ctx_batch_stride, prm, B, st);
+  }
+  // hd = 128: three launches, y through `out` and gated in place — measured faster on B200 than the
+  // gate epilogue there (the fused epilogue lengthens every CTA of the 1.3-wave c2 grid)
+  rc = sk_launch_qkv_prologue(o4, qk_w, freqs, q_buf, k_buf, v_buf, B, L, H, hd, eps, SK_BF16, st);
+  if (rc != SK_OK) return rc;
+  rc = launch_tc<128, false, false>(q_buf, k_buf, v_buf, k_ctx, v_ctx, nullptr, ctx_batch_stride, prm, B, st);
+  if (rc != SK_OK) return rc;
+  return sk_dit_gate(out, o4, out, (long long)B * L, H * hd, SK_BF16, SK_BF16, 1.f, stream);
 }

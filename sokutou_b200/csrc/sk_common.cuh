@@ -30,6 +30,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // A bounded wait gives up after this long; every legitimate wait in these kernels is microseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Programmatic dependent launch for the DiT kernels (each waits for its predecessor with
+// griddepcontrol.wait before reading global memory, so this only moves set-up earlier).
+#ifndef SK_USE_PDL
+#define SK_USE_PDL 1
+#endif
+constexpr bool kUsePdl = SK_USE_PDL != 0;
 
 // ---- mbarrier -------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -101,6 +107,19 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
           "r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
+}
+// Tensor-tile prefetches into L2 (no shared memory, no completion signal).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
 }
 // Untiled bulk copy global -> shared. dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -43,19 +43,33 @@ def cfg_bias(lb: int, tb: int, n_spk: int, seq_len: int, n_text: int, device=Non
 
 
 class DitLayerAttention:
-    """Q/K/V producer + attention of one DiT layer for a fixed (B, L, H, hd, S) shape.
+    """The attention block of one DiT layer for a fixed (B, L, H, hd, S) shape: Q/K/V producer,
+    attention and `gate` consumer (engine/fused.py:293-298), buffers allocated once (before capture).
 
-    `__call__(o4, qk_w, freqs, ctx_k, ctx_v, bias)` returns y (B, L, H, hd) in o4's dtype —
-    the tensor the `gate` kernel consumes. ctx_k/ctx_v: (S, H, hd), the layer's conditioning keys
-    (text then speaker, already k-normed, engine/fast.py:327-338); bias: (B, L + S) or (L + S,).
+    `__call__(o4, qk_w, freqs, ctx_k, ctx_v, bias)` returns y · sigmoid(gate) as (B*L, H*hd) in o4's
+    dtype — the input of the w_o GEMM. ctx_k/ctx_v: (S, H, hd), the layer's conditioning keys (text
+    then speaker, already k-normed, engine/fast.py:327-338); bias: (B, L + S) or (L + S,).
+    bf16 runs the fused block by default (two launches; `fused=False`: the three separate launches,
+    which give the same bits); float32 always runs the three separate launches.
+    `attention(...)` stops before the gate and returns y (B, L, H, hd).
     """
 
-    def __init__(self, B: int, L: int, H: int, hd: int, S: int, dtype: torch.dtype, device, eps: float = 1e-6):
+    def __init__(self, B: int, L: int, H: int, hd: int, S: int, dtype: torch.dtype, device, eps: float = 1e-6,
+                 fused: bool = True):
         self.B, self.L, self.H, self.hd, self.S, self.eps = B, L, H, hd, S, eps
+        self.fused = fused and dtype == torch.bfloat16
         mk = lambda: torch.empty((B, H, L, hd), dtype=dtype, device=device)
         self.q, self.k, self.v = mk(), mk(), mk()
         self.y = torch.empty((B, L, H, hd), dtype=dtype, device=device)
+        self.out = torch.empty((B * L, H * hd), dtype=dtype, device=device)
 
-    def __call__(self, o4, qk_w, freqs, ctx_k, ctx_v, bias):
+    def attention(self, o4, qk_w, freqs, ctx_k, ctx_v, bias):
         ops.dit_qkv_prologue(o4, qk_w, freqs, self.B, self.L, self.H, self.hd, self.eps, out=(self.q, self.k, self.v))
         return ops.dit_attention(self.q, self.k, self.v, ctx_k, ctx_v, bias, out=self.y)
+
+    def __call__(self, o4, qk_w, freqs, ctx_k, ctx_v, bias):
+        if self.fused:
+            return ops.dit_attention_layer(o4, qk_w, freqs, self.B, self.L, self.H, self.hd, self.eps, ctx_k, ctx_v,
+                                           bias, out=self.out, qkv_bufs=(self.q, self.k, self.v))
+        self.attention(o4, qk_w, freqs, ctx_k, ctx_v, bias)
+        return ops.dit_gate(self.y, o4, out=self.out)

@@ -5,6 +5,8 @@ DiT (engine/fused.py:293-298):
     dit_qkv_prologue  — the `qkv` producer (engine/fused.py:117-180) without the per-batch ctx copy
     dit_attention     — the attention over [latent | ctx] keys, y in (B, L, H, hd)
     sdpa              — drop-in for F.scaled_dot_product_attention(q, k, v, attn_mask=bias)
+    dit_gate          — the `gate` consumer (engine/fused.py:182-190): y · sigmoid(gate), optional FP8 out
+    dit_attention_layer — the whole block (producer, attention, gate) in two launches, bf16
 Qwen3 talker (qwen3/kernels.py:622-624):
     decode_attention  — one layer's decode step with the reference kernel's argument list
 """
@@ -16,7 +18,7 @@ import ctypes
 import torch
 
 from . import _lib
-from ._lib import SK_BF16, SK_F32, check, lib
+from ._lib import SK_BF16, SK_E4M3, SK_F32, check, lib
 
 
 def _ptr(t: torch.Tensor | None) -> int:
@@ -143,7 +145,87 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, attn_mask: torch.Ten
     return y.transpose(1, 2)
 
 
+def dit_attention_layer(o4: torch.Tensor, qk_w: torch.Tensor, freqs: torch.Tensor, B: int, L: int, H: int, hd: int,
+                        eps: float, k_ctx: torch.Tensor | None = None, v_ctx: torch.Tensor | None = None,
+                        bias: torch.Tensor | None = None, scale: float | None = None,
+                        out: torch.Tensor | None = None,
+                        qkv_bufs: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+    """One DiT layer's attention block (engine/fused.py:293-298): the `qkv` producer, the attention over
+    [latent | ctx] keys and the `gate` consumer, in two launches (the gate read from o4 by the attention
+    epilogue). o4 (B*L, 4*H*hd) bf16; qk_w float32 (2, H, hd); freqs float32 (>= L, hd/2, 2);
+    k_ctx/v_ctx (S, H, hd) shared or (B, S, H, hd); bias as for dit_attention; qkv_bufs: (B, H, L, hd)
+    bf16 scratch for q, k, v (allocated here when not given). Returns (B*L, H*hd) bf16 =
+    y · sigmoid(gate)."""
+    for n, t in (("o4", o4), ("qk_w", qk_w), ("freqs", freqs)):
+        _cuda_contig(n, t)
+    _need(o4.dtype == torch.bfloat16, "the fused layer runs in bfloat16 (use the separate ops for float32)")
+    D = H * hd
+    _need(o4.shape == (B * L, 4 * D), f"o4 must be ({B * L}, {4 * D}), got {tuple(o4.shape)}")
+    _need(qk_w.dtype == torch.float32 and qk_w.numel() == 2 * D, "qk_w must be float32 (2, H, hd)")
+    _need(freqs.dtype == torch.float32 and freqs.shape[0] >= L and freqs.shape[1:] == (hd // 2, 2),
+          "freqs must be float32 (>= L, hd/2, 2)")
+    S, ctx_bs = 0, 0
+    if k_ctx is not None:
+        _cuda_contig("k_ctx", k_ctx)
+        _cuda_contig("v_ctx", v_ctx)
+        _need(k_ctx.shape == v_ctx.shape and k_ctx.dtype == o4.dtype and v_ctx.dtype == o4.dtype,
+              "k_ctx and v_ctx must match in shape and be bfloat16")
+        if k_ctx.dim() == 3:
+            S = k_ctx.shape[0]
+            _need(k_ctx.shape[1:] == (H, hd), "k_ctx must be (S, H, hd) or (B, S, H, hd)")
+        else:
+            _need(k_ctx.dim() == 4 and k_ctx.shape[0] == B and k_ctx.shape[2:] == (H, hd),
+                  "k_ctx must be (S, H, hd) or (B, S, H, hd)")
+            S, ctx_bs = k_ctx.shape[1], k_ctx.stride(0)
+    K = L + S
+    bias_bs = 0
+    if bias is not None:
+        _cuda_contig("bias", bias)
+        _need(bias.dtype == o4.dtype, "bias must be bfloat16")
+        _need(bias.numel() in (K, B * K), f"bias must hold K={K} or B*K values")
+        bias_bs = K if bias.numel() == B * K else 0
+    if out is None:
+        out = torch.empty((B * L, D), device=o4.device, dtype=o4.dtype)
+    _cuda_contig("out", out)
+    _need(out.numel() == B * L * D and out.dtype == o4.dtype, f"out must hold {B * L}x{D} bfloat16")
+    if qkv_bufs is None:
+        qkv_bufs = tuple(torch.empty((B, H, L, hd), device=o4.device, dtype=o4.dtype) for _ in range(3))
+    for n, t in zip(("q_buf", "k_buf", "v_buf"), qkv_bufs):
+        _cuda_contig(n, t)
+        _need(t.shape == (B, H, L, hd) and t.dtype == o4.dtype, f"{n} must be ({B}, {H}, {L}, {hd}) bfloat16")
+    check(lib().sk_dit_attention_layer(_ptr(o4), _ptr(qk_w), _ptr(freqs), _ptr(k_ctx), _ptr(v_ctx), _ptr(bias),
+                                       _ptr(out), _ptr(qkv_bufs[0]), _ptr(qkv_bufs[1]), _ptr(qkv_bufs[2]), B, H, L,
+                                       S, hd, ctx_bs, bias_bs, float(eps), SK_BF16, float(scale or 0.0), _stream()),
+          "sk_dit_attention_layer")
+    return out
+
+
 # ---- Qwen3 decode --------------------------------------------------------------------------------
+
+def dit_gate(y: torch.Tensor, o4: torch.Tensor, out: torch.Tensor | None = None, fp8_scale: float | None = None
+             ) -> torch.Tensor:
+    """out = y · sigmoid(gate) with gate = o4[:, 3D:4D]; y (B, L, H, hd) or (B·L, D), o4 (B·L, 4·D).
+
+    Returns (B·L, D) in y's dtype, or raw FP8 e4m3 bytes (torch.uint8) of value·fp8_scale when
+    fp8_scale is given (the reference's FP8 GEMM input, engine/fused.py:52-76).
+    """
+    _cuda_contig("y", y)
+    _cuda_contig("o4", o4)
+    _need(y.dtype == o4.dtype, "y and o4 must share a dtype")
+    rows = o4.shape[0]
+    D = o4.shape[1] // 4
+    _need(o4.dim() == 2 and o4.shape[1] == 4 * D and y.numel() == rows * D, "o4 must be (rows, 4*D) and y hold rows*D")
+    code = _dtype_code(y.dtype)
+    out_code = code if fp8_scale is None else SK_E4M3
+    odt = y.dtype if fp8_scale is None else torch.uint8
+    if out is None:
+        out = torch.empty((rows, D), device=y.device, dtype=odt)
+    _cuda_contig("out", out)
+    _need(out.dtype == odt and out.numel() == rows * D, f"out must hold {rows}x{D} {odt}")
+    check(lib().sk_dit_gate(_ptr(y), _ptr(o4), _ptr(out), rows, D, code, out_code,
+                            float(fp8_scale if fp8_scale is not None else 1.0), _stream()), "sk_dit_gate")
+    return out
+
 
 def decode_workspace_bytes(max_len: int, nq: int, nkv: int, hd: int = 128, cache_dtype: torch.dtype = torch.bfloat16) -> int:
     return int(lib().sk_decode_workspace_bytes(max_len, nq, nkv, hd, _dtype_code(cache_dtype)))

@@ -23,6 +23,13 @@ CASES = {
     "dit_c1_L256_b3": ("dit", W.c1(256), 3), "dit_c1_L256_b1": ("dit", W.c1(256), 1),
     "dit_c1_L512_b3": ("dit", W.c1(512), 3), "dit_c1_L512_b1": ("dit", W.c1(512), 1),
     "dit_c2_b3": ("dit", W.C2, 3), "dit_c2_b1": ("dit", W.C2, 1),
+    # one DiT layer's attention block: fused launch vs producer + attention + gate launches
+    "layer_c1_L128_b1_fused": ("layer", W.c1(128), 1), "layer_c1_L128_b1_sep": ("layer_sep", W.c1(128), 1),
+    "layer_c1_L512_b3_fused": ("layer", W.c1(512), 3), "layer_c1_L512_b3_sep": ("layer_sep", W.c1(512), 3),
+    "layer_c2_b3_fused": ("layer", W.C2, 3), "layer_c2_b3_sep": ("layer_sep", W.C2, 3),
+    # the block's two HBM-bound kernels alone
+    "prologue_c1_L512_b3": ("prologue", W.c1(512), 3), "prologue_c2_b3": ("prologue", W.C2, 3),
+    "gate_c1_L512_b3": ("gate", W.c1(512), 3), "gate_c2_b3": ("gate", W.C2, 3),
     "decode_T128": ("decode", 128, None), "decode_T512": ("decode", 512, None),
     "decode_T1120": ("decode", 1120, None), "decode_T1500": ("decode", 1500, None),
     # calibration: what a chain of dependent kernels costs on this GPU without any attention work
@@ -43,6 +50,42 @@ def dit_case(shape, B, sets, dev):
     bias = dit.cfg_bias(L, shape.Tb, shape.Sp, L, 40, device=dev)[:B].contiguous()
     fns = [lambda c=c: ops.dit_attention(c[0], c[1], c[2], c[3], c[4], bias, out=c[5]) for c in calls]
     return fns, shape.flops(B), "flop"
+
+
+def layer_case(shape, B, sets, dev, fused: bool):
+    g = torch.Generator(device=dev).manual_seed(0)
+    H, hd, L, S = shape.H, shape.hd, shape.L, shape.S
+    qk_w = W.dit_qk_weights(shape, dev)
+    freqs = W.dit_freqs(L, hd, device=dev)
+    bias = dit.cfg_bias(L, shape.Tb, shape.Sp, L, 40, device=dev)[:B].contiguous()
+    fns = []
+    for _ in range(sets):
+        o4 = (torch.randn(B * L, 4 * H * hd, device=dev, generator=g) * 0.5).bfloat16()
+        kc = torch.randn(S, H, hd, device=dev, generator=g).bfloat16()
+        vc = torch.randn(S, H, hd, device=dev, generator=g).bfloat16()
+        layer = dit.DitLayerAttention(B, L, H, hd, S, torch.bfloat16, dev, fused=fused)
+        fns.append(lambda o4=o4, kc=kc, vc=vc, layer=layer: layer(o4, qk_w, freqs, kc, vc, bias))
+    return fns, shape.flops(B), "flop"
+
+
+def elementwise_case(kind, shape, B, sets, dev):
+    """The producer (q, k, v from o4) or the gate (y · sigmoid(gate)) of one block; work = bytes moved."""
+    g = torch.Generator(device=dev).manual_seed(0)
+    H, hd, L = shape.H, shape.hd, shape.L
+    qk_w = W.dit_qk_weights(shape, dev)
+    freqs = W.dit_freqs(L, hd, device=dev)
+    fns = []
+    for _ in range(sets):
+        o4 = (torch.randn(B * L, 4 * H * hd, device=dev, generator=g) * 0.5).bfloat16()
+        if kind == "prologue":
+            bufs = tuple(torch.empty(B, H, L, hd, device=dev, dtype=torch.bfloat16) for _ in range(3))
+            fns.append(lambda o4=o4, bufs=bufs: ops.dit_qkv_prologue(o4, qk_w, freqs, B, L, H, hd, 1e-6, out=bufs))
+        else:
+            y = torch.randn(B * L, H * hd, device=dev, generator=g).bfloat16()
+            out = torch.empty_like(y)
+            fns.append(lambda o4=o4, y=y, out=out: ops.dit_gate(y, o4, out=out))
+    moved = B * L * H * hd * 2 * (6 if kind == "prologue" else 3)
+    return fns, moved, "byte"
 
 
 def decode_case(T, sets, dev):
@@ -86,6 +129,10 @@ def main():
     kind, x, B = CASES[a.case]
     if kind == "dit":
         fns, work, unit = dit_case(x, B, a.sets, dev)
+    elif kind in ("prologue", "gate"):
+        fns, work, unit = elementwise_case(kind, x, B, a.sets, dev)
+    elif kind in ("layer", "layer_sep"):
+        fns, work, unit = layer_case(x, B, a.sets, dev, fused=(kind == "layer"))
     elif kind == "decode":
         fns, work, unit = decode_case(x, a.sets, dev)
     else:

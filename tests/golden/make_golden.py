@@ -125,14 +125,17 @@ def make_dit(ref_root):
         ctx_v = torch.randn(n_layers, 1, Tb + Sp, H, hd, generator=g)
         ang = torch.arange(lb, dtype=torch.float64)[:, None] * (1e4 ** (-torch.arange(0, hd, 2, dtype=torch.float64) / hd))
         freqs_c = torch.polar(torch.ones_like(ang), ang).to(torch.complex64)[None, :, None, None, :]
-        rec = {"o": [], "sdpa": []}
+        rec = {"o": [], "sdpa": [], "gated": []}
         orig_linear, orig_sdpa = F.linear, F.scaled_dot_product_attention
         wq = {id(p["w_qkvg"]) for p in core.layers}
+        wo = {id(p["w_o"]) for p in core.layers}
 
         def linear(x_, w, b=None):
             y = orig_linear(x_, w, b)
             if id(w) in wq:
                 rec["o"].append(y.detach().clone())
+            if id(w) in wo:                               # input of w_o = y · sigmoid(gate)
+                rec["gated"].append(x_.detach().clone())
             return y
 
         def sdpa(q, k, v, attn_mask=None, **kw):
@@ -159,6 +162,7 @@ def make_dit(ref_root):
             q=q.contiguous().numpy(), k=k.contiguous().numpy(),           # as SDPA receives them: (B, H, *, hd)
             v=v.contiguous().numpy(), mask=m.reshape(B, -1).numpy(),
             y=y.transpose(1, 2).contiguous().numpy(),     # (B, L, H, hd)
+            gated=rec["gated"][li].reshape(B * lb, dim).numpy(),  # engine/fast.py:174, the `gate` output
             mask3=mask3, bias3=bias3,
         )
     # Extra mask cases (padding in every segment, single text token, full text bucket).

@@ -81,7 +81,7 @@ def _config_case(cuda, shape, B, dt, seed):
     freqs = W.dit_freqs(shape.L, shape.hd, device=cuda)
     layer = dit.DitLayerAttention(B, shape.L, shape.H, shape.hd, shape.S, dt, cuda)
     bias = x["bias3"][:B].contiguous()
-    y = layer(x["o4"], qk_w, freqs, x["ctx_k"], x["ctx_v"], bias)
+    y = layer.attention(x["o4"], qk_w, freqs, x["ctx_k"], x["ctx_v"], bias)
     torch.cuda.synchronize()
     ref = D.dit_attention(host(layer.q), host(layer.k), host(layer.v), host(x["ctx_k"])[None], host(x["ctx_v"])[None],
                           host(bias))
@@ -186,15 +186,15 @@ def test_graph_capture_replays(cuda):
     layer = dit.DitLayerAttention(3, shape.L, shape.H, shape.hd, shape.S, torch.bfloat16, cuda)
     args = (x["o4"], W.dit_qk_weights(shape, cuda), W.dit_freqs(shape.L, shape.hd, device=cuda), x["ctx_k"],
             x["ctx_v"], x["bias3"])
-    y0 = layer(*args).clone()
+    y0 = layer.attention(*args).clone()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        layer(*args)
+        layer.attention(*args)
     torch.cuda.current_stream().wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        layer(*args)
+        layer.attention(*args)
     layer.y.zero_()
     g.replay()
     torch.cuda.synchronize()

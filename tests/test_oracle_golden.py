@@ -89,3 +89,37 @@ def test_fully_masked_rows_give_zero():
     k = rng.standard_normal((1, 1, 5, 8))
     y = D.dit_attention(q, k, k, bias=np.full((1, 5), -np.inf))
     assert np.all(y == 0)
+
+
+@pytest.mark.parametrize("case", ["dit_small", "dit_hd128"])
+def test_gate_matches_reference(case):
+    """The `gate` consumer (engine/fused.py:182-190) against the reference DiT core's own product
+    y · sigmoid(gate) (engine/fast.py:174), recorded at the input of w_o."""
+    g = load_golden(case)
+    out = D.gate(g["y"], g["o4"], "f32")
+    assert rel_l2(out, g["gated"]) < 1e-6
+
+
+def test_e4m3_encoder_known_values():
+    """FP8 e4m3 as the reference writes it (engine/fused.py:60-72): nearest even, ±448 saturation,
+    subnormal step 2^-9, NaN -> 0x7f, signed zero kept."""
+    x = np.array([0.0, -0.0, 1.0, -1.0, 1.0625, 1.1875, 448.0, 449.0, 1e6, float("inf"), float("-inf"),
+                  2.0 ** -9, 2.0 ** -10, 3 * 2.0 ** -10, 2.0 ** -6, float("nan"), 0.3], np.float32)
+    want = np.array([0x00, 0x80, 0x38, 0xB8, 0x38, 0x3A, 0x7E, 0x7E, 0x7E, 0x7E, 0xFE,
+                     0x01, 0x00, 0x02, 0x08, 0x7F, 0x2A], np.uint8)
+    assert np.array_equal(D.e4m3_encode(x), want)
+    codes = np.arange(256, dtype=np.uint8)
+    finite = (codes & 0x7F) != 0x7F
+    assert np.array_equal(D.e4m3_encode(D.e4m3_decode(codes[finite])), codes[finite])  # round trip
+
+
+@pytest.mark.parametrize("case", ["dit_small", "dit_hd128"])
+def test_attention_layer_oracle_matches_reference(case):
+    """producer -> SDPA -> gate composed (engine/fused.py:293-298) against the reference DiT core's gated
+    output: float32 path within 1e-5, bf16-rounded path within the bf16 bar."""
+    g = load_golden(case)
+    H, hd, L = int(g["H"]), int(g["hd"]), int(g["L"])
+    args = (g["o4"], g["qk_w"], g["freqs"], 3, L, H, hd, float(g["qk_eps"]), g["ctx_k"][None], g["ctx_v"][None],
+            g["bias3"])
+    assert rel_l2(D.attention_layer(*args, bf16=False), g["gated"]) < FP32_TOL
+    assert rel_l2(D.attention_layer(*args, bf16=True), g["gated"]) < 1e-2
