@@ -137,30 +137,6 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
 #define SK_POLY_PAIRS 0
 #endif
 constexpr int kPolyPairs = SK_POLY_PAIRS;
-// 1: softmax exponentials as packed bf16 pairs (ex2.approx.ftz.bf16x2), half the MUFU operations.
-#ifndef SK_EXP_BF16X2
-#define SK_EXP_BF16X2 0
-#endif
-// The producer issues V_j only after K_{j+kKLead}: S = Q·Kᵀ needs its K tile one softmax earlier
-// than P·V needs the matching V tile, so K loads go first when many copies compete for DRAM.
-#ifndef SK_K_LEAD
-#define SK_K_LEAD 0
-#endif
-constexpr int kKLead = SK_K_LEAD;
-// Key tiles from this index on are prefetched into L2 (K and V, in the order they are needed) right
-// after Q is requested, so that their ring loads later hit L2 instead of waiting on DRAM; 0 = off.
-#ifndef SK_L2_PREFETCH_FROM
-#define SK_L2_PREFETCH_FROM 0
-#endif
-constexpr int kL2PrefetchFrom = SK_L2_PREFETCH_FROM;
-// Back-off (ns) of the polling producer and MMA threads after a pass that found nothing to issue;
-// their spins share issue slots with the softmax warps of the same sub-partition.
-#ifndef SK_PRODUCER_SLEEP_NS
-#define SK_PRODUCER_SLEEP_NS 0
-#endif
-#ifndef SK_MMA_SLEEP_NS
-#define SK_MMA_SLEEP_NS 0
-#endif
 
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
   asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
@@ -293,20 +269,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int c = 0; c < Ly::NCH; ++c) tma_prefetch_l2_3d(&tmG, 3 * prm.D + h * HD + c * 64, q0, b);
       }
-      if (kL2PrefetchFrom > 0) {
-        for (int j = kL2PrefetchFrom; j < ntiles; ++j) {
-#pragma unroll
-          for (int c = 0; c < Ly::NCH; ++c) {
-            if (j < n_lat) {
-              tma_prefetch_l2_3d(&tmK, c * 64, j * kBN, lz);
-              tma_prefetch_l2_3d(&tmV, xv + c * 64, j * kBN, lzv);
-            } else {
-              tma_prefetch_l2_4d(&tmKc, c * 64, h, (j - n_lat) * kBN, bc);
-              tma_prefetch_l2_4d(&tmVc, c * 64, h, (j - n_lat) * kBN, bc);
-            }
-          }
-        }
-      }
       int jk = 0, jv = 0;
       bool ok = true;
       const uint64_t t0 = globaltimer_ns();
@@ -329,8 +291,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           ++jk;
           progress = true;
         }
-        if (jv < ntiles && (jk > jv + kKLead || jk == ntiles) &&
-            (jv < NSV || mbar_test(&v_empty[jv % NSV], ((jv / NSV) - 1) & 1))) {
+        if (jv < ntiles && jv < jk && (jv < NSV || mbar_test(&v_empty[jv % NSV], ((jv / NSV) - 1) & 1))) {
           const int s = jv % NSV;
           uint8_t* dst = smem + Ly::OFF_V + s * Ly::KV_BYTES;
           mbar_arrive_expect_tx(&v_full[s], Ly::KV_BYTES);
@@ -346,12 +307,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           ++jv;
           progress = true;
         }
-        if (!progress) {
-          if (SK_PRODUCER_SLEEP_NS > 0) __nanosleep(SK_PRODUCER_SLEEP_NS);
-          if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-            set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
-            ok = false;
-          }
+        if (!progress && (++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
+          ok = false;
         }
       }
       // fused: the gate tile goes where Q was, once no MMA reads Q any more (a blocking wait: the
@@ -426,12 +384,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           ++jp;
           progress = true;
         }
-        if (!progress) {
-          if (SK_MMA_SLEEP_NS > 0) __nanosleep(SK_MMA_SLEEP_NS);
-          if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-            set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
-            ok = false;
-          }
+        if (!progress && (++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
+          ok = false;
         }
       }
       tc_commit(mma_done);
@@ -519,34 +474,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       const float2 nm = make_float2(-m_use, -m_use);
-#if SK_EXP_BF16X2
-      // exponentials two at a time on packed bf16: d = t - m in fp32, rounded to bf16x2, one
-      // ex2.approx.ftz.bf16x2 per pair gives the packed P operand directly; the row sum adds the
-      // same bf16 values the P·V product uses
-      uint32_t pq[kBN / 2];
-#pragma unroll
-      for (int i = 0; i < kBN / 2; ++i) {
-        const float2 dd = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nm);
-        const __nv_bfloat162 db = __floats2bfloat162_rn(dd.x, dd.y);
-        asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(pq[i]) : "r"(*reinterpret_cast<const uint32_t*>(&db)));
-      }
-      float2 ls0 = make_float2(0.f, 0.f), ls1 = ls0;
-#pragma unroll
-      for (int u = 0; u < kBN / 8; ++u) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t w = pq[4 * u + e];
-          const float2 p = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-          if (e & 1)
-            ls1 = __fadd2_rn(ls1, p);
-          else
-            ls0 = __fadd2_rn(ls0, p);
-        }
-        const int chunk = u >> 3, unit = u & 7;
-        *reinterpret_cast<uint4*>(prow + chunk * (kBM * 128) + ((unit ^ (row & 7)) << 4)) =
-            make_uint4(pq[4 * u], pq[4 * u + 1], pq[4 * u + 2], pq[4 * u + 3]);
-      }
-#else
       // pass 1: all 128 exponentials in place (independent, so the MUFU pipe stays fed)
 #pragma unroll
       for (int c = 0; c < kBN; c += 8) {
@@ -577,7 +504,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         *reinterpret_cast<uint4*>(prow + chunk * (kBM * 128) + ((unit ^ (row & 7)) << 4)) =
             make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-#endif
       l_run += (ls0.x + ls0.y) + (ls1.x + ls1.y);
       fence_proxy_async_smem();
       tc_fence_before();

@@ -76,9 +76,7 @@ __global__ void __launch_bounds__(kPrologueThreads) qkv_prologue_kernel(const T*
   // o4 may be written by the kernel launched before this one (programmatic dependent launch); the
   // weights and the table are constants of the model
   asm volatile("griddepcontrol.wait;" ::: "memory");
-#ifndef SK_PROLOGUE_LATE_TRIGGER
   asm volatile("griddepcontrol.launch_dependents;");
-#endif
   const int row = blockIdx.x * (kPrologueThreads / 32) + warp;
   const int b = row / L, p = row - b * L;
   const int qk_chunks = 2 * H * NV;
