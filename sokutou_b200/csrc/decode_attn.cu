@@ -369,11 +369,6 @@ __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("grid
 
 constexpr int kMaxCluster = 16;
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
 __device__ __forceinline__ uint32_t cluster_size_reg() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
@@ -383,38 +378,10 @@ __device__ __forceinline__ void cluster_arrive_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
-// Address of `p` (this CTA's shared memory) in the shared memory of cluster rank `rank`.
-__device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
-}
 __device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
-}
-// Bounded wait with cluster-scope acquire: the arrivals came from other CTAs of the cluster.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 0;; ++i) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if ((i & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) {
-      set_dev_error(err, SK_DEVERR_TIMEOUT);
-      return false;
-    }
-  }
-}
 
 template <typename CT>
 struct Vec4;  // four consecutive cache elements as one shared-memory load
@@ -431,17 +398,6 @@ struct Vec4<float> {
   static __device__ __forceinline__ float4 ld(const float* p) { return *reinterpret_cast<const float4*>(p); }
 };
 
-__device__ __forceinline__ void st_async(uint32_t remote_addr, float v, uint32_t remote_bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(remote_addr), "f"(v),
-               "r"(remote_bar)
-               : "memory");
-}
-__device__ __forceinline__ void st_async4(uint32_t remote_addr, float4 v, uint32_t remote_bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-                   remote_addr),
-               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
-               : "memory");
-}
 
 constexpr int kThreadsCl = 256;  // 8 warps: two per scheduler, so dependent chains overlap
 constexpr int kPartialBytes = kG * kHD * 4 + kG * 2 * 4;  // one CTA's (o, max, sum) for rank 0
