@@ -367,7 +367,9 @@ class DecodeBench:
     def step(self):
         for ta in self.ta:
             for li in range(self.s.n_layers):
-                ta.attn(li, self.qkv[li], self.qn[li], self.kn[li], self.out[li])
+                # layer 0 follows the position advance; the others follow a kernel that writes neither
+                # the position nor their cache (the layer's qkv projection, at the reference call site)
+                ta.attn(li, self.qkv[li], self.qn[li], self.kn[li], self.out[li], kv_stable=li > 0)
             ta.pos.add_(1)
 
     def reset(self):

@@ -189,6 +189,25 @@ SK_API int sk_decode_attention(const float* qkv, const float* qn, const float* k
                         float* out, void* workspace, size_t ws_bytes, int cache_dtype, void* stream);
 
 /*
+ * sk_decode_attention with launch options (`flags`, a bit set; 0 gives exactly sk_decode_attention):
+ *
+ *   SK_DECODE_KV_STABLE — the caller promises that the kernel launched immediately before this call
+ *     on the stream writes neither pos_ptr[0] nor this layer's cache rows [0, pos). The kernel then
+ *     reads the position and issues the copies of its K/V chunk before waiting for that kernel
+ *     (programmatic dependent launch), so the cache reads overlap that kernel's tail; qkv, qn and kn
+ *     are still read only after it has finished. True at the reference's call site, where the
+ *     attention follows the layer's rms_gemv (qwen3/kernels.py:619-627); not for the first layer
+ *     right after the kernel that advances the position.
+ * No counterpart in the reference (its kernel has no launch options).
+ */
+#define SK_DECODE_KV_STABLE 1
+SK_API int sk_decode_attention_ex(const float* qkv, const float* qn, const float* kn, float eps,
+                                  const float* rope, void* Kc, void* Vc,
+                                  const long long* pos_ptr, int pos_add, int max_len, int nq, int nkv, int hd,
+                                  float* out, void* workspace, size_t ws_bytes, int cache_dtype, int flags,
+                                  void* stream);
+
+/*
  * sk_decode_attention without a workspace argument: allocates nothing, for callers that cannot call
  * cudaMalloc when they attend (a serving process that reserves its device memory up front and
  * forbids allocation afterwards, a driver running inside a CUDA graph capture, a foreign-language

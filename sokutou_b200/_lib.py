@@ -19,6 +19,7 @@ ERRORS = {-1: "SK_ERR_INVALID_ARG", -2: "SK_ERR_UNSUPPORTED", -3: "SK_ERR_CUDA",
           -5: "SK_ERR_WORKSPACE", -6: "SK_ERR_TOO_LARGE"}
 DEVICE_ERRORS = {0: "SK_DEVERR_NONE", 1: "SK_DEVERR_POS_RANGE", 2: "SK_DEVERR_TIMEOUT"}
 SK_BF16, SK_F32, SK_E4M3 = 0, 1, 2
+SK_DECODE_KV_STABLE = 1
 
 # every symbol the header declares, with (restype, argtypes)
 _P, _I, _F, _LL, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_longlong, ctypes.c_size_t
@@ -32,6 +33,7 @@ SIGNATURES = {
                                     _F, _P]),
     "sk_decode_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "sk_decode_attention": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _P]),
+    "sk_decode_attention_ex": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _I, _P]),
     "sk_decode_attention_noalloc": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P]),
 }
 

@@ -410,7 +410,10 @@ constexpr int kPartialBytes = kG * kHD * 4 + kG * 2 * 4;  // one CTA's (o, max, 
 // fence or barrier across the cluster on the way out.
 // griddepcontrol.wait precedes every global read (pos, qkv, cache), so under programmatic dependent
 // launch only the CTA set-up overlaps the kernel before.
-template <typename CT>
+// EARLY: the position and this layer's cache rows before it are not written by the kernel launched
+// just before this one, so the position is read and the K/V chunk copies are issued before
+// griddepcontrol.wait — they overlap that kernel's tail; only qkv, qn and kn wait for it.
+template <typename CT, bool EARLY>
 __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
     const float* __restrict__ qkv, const float* __restrict__ qn, const float* __restrict__ kn, float eps,
     const float* __restrict__ rope, CT* __restrict__ Kc, CT* __restrict__ Vc, const long long* __restrict__ pos_ptr,
@@ -446,30 +449,39 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
   __syncthreads();
   cluster_arrive_relaxed();  // matched by cluster_wait() before the first push into rank 0
   if (rank == 0 && t == 0) mbar_arrive_expect_tx(&mrg_bar, (uint32_t)(CL * kPartialBytes));
+  // The position, this CTA's share of the keys, and the bulk copies of its K/V chunk (the new row is
+  // appended below, not copied).
+  int pos = 0, T = 0, chunk = 0, s0 = 0, n = 0, n_ld = 0;
+  bool owner = false;
+  const size_t head_base = (size_t)kvh * max_len * kHD;
+  auto issue_kv = [&]() -> bool {
+    pos = (pos_ptr ? (int)pos_ptr[0] : 0) + pos_add;
+    if (pos < 0 || pos >= max_len) {  // every CTA of every cluster reads the same pos: all leave here
+      if (rank == 0 && kvh == 0 && t == 0) set_dev_error(err, SK_DEVERR_POS_RANGE);
+      return false;
+    }
+    T = pos + 1;
+    chunk = (T + CL - 1) / CL;
+    s0 = rank * chunk;
+    n = max(0, min(chunk, T - s0));  // keys of this CTA (0 for ranks past T)
+    owner = n > 0 && (s0 + n == T);  // holds the new position
+    n_ld = owner ? n - 1 : n;
+    if (t == 0 && n_ld > 0) {
+      const uint32_t bytes = (uint32_t)(n_ld * kHD * sizeof(CT));
+      mbar_arrive_expect_tx(&bar, 2 * bytes);
+      bulk_load(Ks, Kc + head_base + (size_t)s0 * kHD, bytes, &bar);
+      bulk_load(Vs, Vc + head_base + (size_t)s0 * kHD, bytes, &bar);
+    }
+    return true;
+  };
+  if (EARLY && !issue_kv()) return;
   griddep_wait();
   griddep_launch_dependents();
   // loads that do not depend on the position go out together with it
   const float qv = qkv[(size_t)(kvh * kG + g_t) * kHD + d];
   const float xv = qkv[(size_t)(nq + g_t * nkv) * kHD + (size_t)kvh * kHD + d];  // k (g_t = 0) or v (g_t = 1)
   const float qn_d = qn[d], kn_d = kn[d];
-  const int pos = (pos_ptr ? (int)pos_ptr[0] : 0) + pos_add;
-  if (pos < 0 || pos >= max_len) {  // every CTA of every cluster reads the same pos: all leave here
-    if (rank == 0 && kvh == 0 && t == 0) set_dev_error(err, SK_DEVERR_POS_RANGE);
-    return;
-  }
-  const int T = pos + 1;
-  const int chunk = (T + CL - 1) / CL;
-  const int s0 = rank * chunk;
-  const int n = max(0, min(chunk, T - s0));  // keys of this CTA (0 for ranks past T)
-  const bool owner = n > 0 && (s0 + n == T);  // holds the new position
-  const int n_ld = owner ? n - 1 : n;
-  const size_t head_base = (size_t)kvh * max_len * kHD;
-  if (t == 0 && n_ld > 0) {
-    const uint32_t bytes = (uint32_t)(n_ld * kHD * sizeof(CT));
-    mbar_arrive_expect_tx(&bar, 2 * bytes);
-    bulk_load(Ks, Kc + head_base + (size_t)s0 * kHD, bytes, &bar);
-    bulk_load(Vs, Vc + head_base + (size_t)s0 * kHD, bytes, &bar);
-  }
+  if (!EARLY && !issue_kv()) return;
   const float c = rope[(size_t)pos * kHD + (d & 63)];
   const float s = rope[(size_t)pos * kHD + 64 + (d & 63)];
 
@@ -652,9 +664,11 @@ static int cluster_size(int nkv, size_t smem) {
   const int ti = sizeof(CT) == 2 ? 0 : 1;
   std::lock_guard<std::mutex> lk(mu);
   if (cached_smem[dev][ti] == smem && cached_cl[dev][ti] != 0) return cached_cl[dev][ti];
-  auto kfn = decode_attn_cluster_kernel<CT>;
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
-  cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  auto kfn = decode_attn_cluster_kernel<CT, false>;
+  for (auto f : {decode_attn_cluster_kernel<CT, false>, decode_attn_cluster_kernel<CT, true>}) {
+    if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  }
   int chosen = 0;
   for (int cl : {16, 8}) {
     cudaLaunchConfig_t cfg = {};
@@ -683,7 +697,7 @@ static int cluster_size(int nkv, size_t smem) {
 template <typename CT>
 static int launch_cluster(const float* qkv, const float* qn, const float* kn, float eps, const float* rope, void* Kc,
                           void* Vc, const long long* pos_ptr, int pos_add, int max_len, int nq, int nkv, float* out,
-                          int* err, cudaStream_t st) {
+                          int* err, bool early, cudaStream_t st) {
   // the shared memory of the largest chunk decides whether one cluster per kv head can hold T = max_len
   for (int cl : {16, 8}) {
     const int chunk_max = (max_len + cl - 1) / cl;
@@ -705,9 +719,14 @@ static int launch_cluster(const float* qkv, const float* qn, const float* kn, fl
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    if (cudaLaunchKernelEx(&cfg, decode_attn_cluster_kernel<CT>, qkv, qn, kn, eps, rope, reinterpret_cast<CT*>(Kc),
-                           reinterpret_cast<CT*>(Vc), pos_ptr, pos_add, max_len, nq, nkv, out, err) != cudaSuccess)
-      return SK_ERR_CUDA;
+    const cudaError_t e =
+        early ? cudaLaunchKernelEx(&cfg, decode_attn_cluster_kernel<CT, true>, qkv, qn, kn, eps, rope,
+                                   reinterpret_cast<CT*>(Kc), reinterpret_cast<CT*>(Vc), pos_ptr, pos_add, max_len, nq,
+                                   nkv, out, err)
+              : cudaLaunchKernelEx(&cfg, decode_attn_cluster_kernel<CT, false>, qkv, qn, kn, eps, rope,
+                                   reinterpret_cast<CT*>(Kc), reinterpret_cast<CT*>(Vc), pos_ptr, pos_add, max_len, nq,
+                                   nkv, out, err);
+    if (e != cudaSuccess) return SK_ERR_CUDA;
     return SK_OK;
   }
   return SK_ERR_UNSUPPORTED;
@@ -724,10 +743,12 @@ extern "C" size_t sk_decode_workspace_bytes(int max_len, int nq, int nkv, int hd
   return decode::ws_bytes(max_len, nkv);
 }
 
-extern "C" int sk_decode_attention(const float* qkv, const float* qn, const float* kn, float eps, const float* rope,
-                                   void* Kc, void* Vc, const long long* pos_ptr, int pos_add, int max_len, int nq,
-                                   int nkv, int hd, float* out, void* workspace, size_t ws_bytes, int cache_dtype,
-                                   void* stream) {
+extern "C" int sk_decode_attention_ex(const float* qkv, const float* qn, const float* kn, float eps,
+                                      const float* rope, void* Kc, void* Vc, const long long* pos_ptr, int pos_add,
+                                      int max_len, int nq, int nkv, int hd, float* out, void* workspace,
+                                      size_t ws_bytes, int cache_dtype, int flags, void* stream) {
+  if (flags & ~SK_DECODE_KV_STABLE) return SK_ERR_INVALID_ARG;
+  const bool early = (flags & SK_DECODE_KV_STABLE) != 0;
   if (!qkv || !qn || !kn || !rope || !Kc || !Vc || !out) return SK_ERR_INVALID_ARG;
   if (max_len <= 0 || nkv <= 0 || nq <= 0) return SK_ERR_INVALID_ARG;
   if (hd != decode::kHD || nq != decode::kG * nkv) return SK_ERR_UNSUPPORTED;
@@ -746,9 +767,9 @@ extern "C" int sk_decode_attention(const float* qkv, const float* qn, const floa
   if (max_len > decode::kChunk) {
     rc = cache_dtype == SK_BF16
              ? decode::launch_cluster<__nv_bfloat16>(qkv, qn, kn, eps, rope, Kc, Vc, pos_ptr, pos_add, max_len, nq,
-                                                      nkv, out, err, st)
+                                                      nkv, out, err, early, st)
              : decode::launch_cluster<float>(qkv, qn, kn, eps, rope, Kc, Vc, pos_ptr, pos_add, max_len, nq, nkv,
-                                             out, err, st);
+                                             out, err, early, st);
     if (rc != SK_ERR_UNSUPPORTED) return rc;  // else: too long for one cluster, use the workspace kernel
   }
   dim3 grid(nsplit, nkv), block(decode::kThreads);
@@ -773,6 +794,14 @@ extern "C" int sk_decode_attention(const float* qkv, const float* qn, const floa
                                                                   max_len, nq, nkv, out, workspace, err);
   }
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
+}
+
+extern "C" int sk_decode_attention(const float* qkv, const float* qn, const float* kn, float eps, const float* rope,
+                                   void* Kc, void* Vc, const long long* pos_ptr, int pos_add, int max_len, int nq,
+                                   int nkv, int hd, float* out, void* workspace, size_t ws_bytes, int cache_dtype,
+                                   void* stream) {
+  return sk_decode_attention_ex(qkv, qn, kn, eps, rope, Kc, Vc, pos_ptr, pos_add, max_len, nq, nkv, hd, out,
+                                workspace, ws_bytes, cache_dtype, 0, stream);
 }
 
 // ---- Allocation-free variant ------------------------------------------------------------------------

@@ -240,9 +240,13 @@ def decode_workspace(max_len: int, nq: int, nkv: int, device, hd: int = 128,
 
 def decode_attention(qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps: float, rope: torch.Tensor,
                      Kc: torch.Tensor, Vc: torch.Tensor, pos_ptr: torch.Tensor | None, pos_add: int, max_len: int,
-                     nq: int, nkv: int, out: torch.Tensor, workspace: torch.Tensor | None) -> torch.Tensor:
+                     nq: int, nkv: int, out: torch.Tensor, workspace: torch.Tensor | None,
+                     kv_stable: bool = False) -> torch.Tensor:
     """One talker layer's decode attention with the reference kernel's arguments
-    (qwen3/kernels.py:341-344): writes K/V at pos = pos_ptr[0] + pos_add and out (nq*128 fp32)."""
+    (qwen3/kernels.py:341-344): writes K/V at pos = pos_ptr[0] + pos_add and out (nq*128 fp32).
+
+    kv_stable: the kernel launched just before on this stream writes neither the position nor this
+    layer's cache, so the cache reads may overlap it (SK_DECODE_KV_STABLE)."""
     hd = Kc.shape[-1]
     for n, t in (("qkv", qkv), ("qn", qn), ("kn", kn), ("rope", rope), ("Kc", Kc), ("Vc", Vc), ("out", out)):
         _cuda_contig(n, t)
@@ -254,9 +258,11 @@ def decode_attention(qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps:
     if pos_ptr is not None:
         _need(pos_ptr.is_cuda and pos_ptr.dtype == torch.int64, "pos_ptr must be a CUDA int64 tensor")
     ws_n = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    check(lib().sk_decode_attention(_ptr(qkv), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
-                                    _ptr(pos_ptr), int(pos_add), int(max_len), int(nq), int(nkv), int(hd), _ptr(out),
-                                    _ptr(workspace), ws_n, _dtype_code(Kc.dtype), _stream()), "sk_decode_attention")
+    check(lib().sk_decode_attention_ex(_ptr(qkv), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
+                                       _ptr(pos_ptr), int(pos_add), int(max_len), int(nq), int(nkv), int(hd),
+                                       _ptr(out), _ptr(workspace), ws_n, _dtype_code(Kc.dtype),
+                                       _lib.SK_DECODE_KV_STABLE if kv_stable else 0, _stream()),
+          "sk_decode_attention")
     return out
 
 

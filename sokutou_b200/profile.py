@@ -32,6 +32,7 @@ CASES = {
     "gate_c1_L512_b3": ("gate", W.c1(512), 3), "gate_c2_b3": ("gate", W.C2, 3),
     "decode_T128": ("decode", 128, None), "decode_T512": ("decode", 512, None),
     "decode_T1120": ("decode", 1120, None), "decode_T1500": ("decode", 1500, None),
+    "decode_T1120_kvstable": ("decode", 1120, "kv_stable"), "decode_T128_kvstable": ("decode", 128, "kv_stable"),
     # calibration: what a chain of dependent kernels costs on this GPU without any attention work
     "calib_tiny": ("calib", 0, None), "calib_copy_4.6MB": ("calib", 4616192, None),
 }
@@ -88,7 +89,7 @@ def elementwise_case(kind, shape, B, sets, dev):
     return fns, moved, "byte"
 
 
-def decode_case(T, sets, dev):
+def decode_case(T, sets, dev, kv_stable=False):
     s = W.C3
     max_len = 1536
     g = torch.Generator(device=dev).manual_seed(0)
@@ -101,7 +102,7 @@ def decode_case(T, sets, dev):
         qkv = torch.randn((s.nq + 2 * s.nkv) * s.hd, device=dev, generator=g)
         qn = torch.ones(s.hd, device=dev)
         out = torch.empty(s.nq * s.hd, device=dev)
-        fns.append(lambda ta=ta, qkv=qkv, qn=qn, out=out: ta.attn(0, qkv, qn, qn, out))
+        fns.append(lambda ta=ta, qkv=qkv, qn=qn, out=out: ta.attn(0, qkv, qn, qn, out, kv_stable=kv_stable))
     return fns, s.layer_bytes(T), "byte"
 
 
@@ -134,7 +135,7 @@ def main():
     elif kind in ("layer", "layer_sep"):
         fns, work, unit = layer_case(x, B, a.sets, dev, fused=(kind == "layer"))
     elif kind == "decode":
-        fns, work, unit = decode_case(x, a.sets, dev)
+        fns, work, unit = decode_case(x, a.sets, dev, kv_stable=(B == "kv_stable"))
     else:
         fns, work, unit = calib_case(x, a.sets, dev)
     for f in fns:

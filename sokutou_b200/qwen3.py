@@ -39,6 +39,8 @@ class TalkerAttention:
         self.ws = ops.decode_workspace(max_len, nq, nkv, device, hd, cache_dtype)
 
     def attn(self, layer: int, qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, out: torch.Tensor,
-             pos_add: int = 0) -> torch.Tensor:
+             pos_add: int = 0, kv_stable: bool = False) -> torch.Tensor:
+        """kv_stable: the kernel launched just before writes neither self.pos nor this layer's cache (true
+        after the layer's qkv projection; false right after the position advance)."""
         return ops.decode_attention(qkv, qn, kn, self.eps, self.rope, self.k[layer], self.v[layer], self.pos, pos_add,
-                                    self.max_len, self.nq, self.nkv, out, self.ws)
+                                    self.max_len, self.nq, self.nkv, out, self.ws, kv_stable)

@@ -220,7 +220,7 @@ class GpuExecutor:
 
         def run():
             for li in range(s.n_layers):
-                ta.attn(li, qkv[li], qn[li], kn[li], out[li])
+                ta.attn(li, qkv[li], qn[li], kn[li], out[li], kv_stable=li > 0)
             ta.pos.add_(1)
 
         ta.pos.fill_(s.prompt)

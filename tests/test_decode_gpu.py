@@ -217,3 +217,46 @@ def test_bf16_layer_outputs_teacher_forced(cuda):
             h = h + w["w_o"][li] @ att
         ta.pos.add_(1)
     assert worst < BF16_TOL
+
+
+@pytest.mark.parametrize("cache", ["bf16", "f32"])
+def test_kv_stable_launch_gives_same_bits(cuda, cache):
+    """SK_DECODE_KV_STABLE only moves the position read and the cache copies before the wait for the
+    previous kernel: a graph-replayed 4-layer stack (layer 0 after the position advance, the others
+    flagged) must give the same outputs and caches, bit for bit, as the plain launches."""
+    s = W.C3
+    n_layers, max_len, steps = 4, 512, 6
+    res = {}
+    for flagged in (False, True):
+        g = torch.Generator(device=cuda).manual_seed(11)
+        ta = qwen3.TalkerAttention(n_layers, s.nq, s.nkv, max_len, s.theta, s.eps, cuda, CDT[cache])
+        ta.k.copy_(torch.randn(ta.k.shape, device=cuda, generator=g))
+        ta.v.copy_(torch.randn(ta.v.shape, device=cuda, generator=g))
+        qkv = torch.randn(n_layers, (s.nq + 2 * s.nkv) * s.hd, device=cuda, generator=g)
+        qn = 1 + 0.02 * torch.randn(n_layers, s.hd, device=cuda, generator=g)
+        out = torch.empty(steps, n_layers, s.nq * s.hd, device=cuda)
+
+        def step(o):
+            for li in range(n_layers):
+                ta.attn(li, qkv[li], qn[li], qn[li], o[li], kv_stable=flagged and li > 0)
+            ta.pos.add_(1)
+
+        ta.pos.fill_(300)
+        buf = torch.empty(n_layers, s.nq * s.hd, device=cuda)
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            step(buf)
+        torch.cuda.current_stream().wait_stream(st)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            step(buf)
+        ta.pos.fill_(310)
+        for i in range(steps):
+            gr.replay()
+            out[i].copy_(buf)
+        torch.cuda.synchronize()
+        assert ops.device_error() == 0
+        res[flagged] = (out.cpu(), ta.k.float().cpu(), ta.v.float().cpu())
+    for a, b in zip(res[False], res[True]):
+        assert torch.equal(a, b)
