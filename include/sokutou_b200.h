@@ -208,6 +208,25 @@ SK_API int sk_decode_attention_ex(const float* qkv, const float* qn, const float
                                   void* stream);
 
 /*
+ * Qwen3 prefill attention: the prompt's causal self-attention, which the reference runs inside the HF
+ * talker with SDPA (qwen3/fast.py:251-263), on the tensor-core kernel with a causal mask and GQA.
+ * For every prompt token t in [0, T) at position pos0 + t:
+ *   - q heads RMS-normalised (× qn) and rotated (rotate-half RoPE from `rope`, as sk_decode_attention),
+ *     k normalised (× kn) and rotated, v raw; k and v appended to the caches at row pos0 + t (the bits
+ *     decode steps would write);
+ *   - out[t] = softmax(q·kᵀ / sqrt(128)) · v over the cache rows [0, pos0 + t] of the key/value head
+ *     h / 2 (earlier rows pos0 > 0: a prompt chunk after a cached prefix).
+ *   qkv   : fp32 (T, (nq + 2*nkv) * 128) rows = [q heads | k heads | v heads] per token
+ *   Kc, Vc: this layer's cache [nkv][max_len][128], bf16 (cache_dtype SK_BF16 only)
+ *   out   : (T, nq * 128) bf16;  q_buf: caller scratch (nq, T, 128) bf16
+ *   hd = 128, nq = 2*nkv, pos0 + T <= max_len; buffers 16-byte aligned.
+ */
+SK_API int sk_prefill_attention(const float* qkv, const float* qn, const float* kn, float eps,
+                                const float* rope, void* Kc, void* Vc, int pos0, int T, int max_len,
+                                int nq, int nkv, int hd, void* out, void* q_buf, int cache_dtype,
+                                void* stream);
+
+/*
  * sk_decode_attention without a workspace argument: allocates nothing, for callers that cannot call
  * cudaMalloc when they attend (a serving process that reserves its device memory up front and
  * forbids allocation afterwards, a driver running inside a CUDA graph capture, a foreign-language

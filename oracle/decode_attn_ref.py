@@ -80,6 +80,15 @@ def decode_step(qkv, qn, kn, eps, rope, Kc, Vc, pos: int, nq: int, nkv: int, cac
     return out.reshape(-1)
 
 
+def prefill(qkv_rows, qn, kn, eps, rope, Kc, Vc, pos0: int, nq: int, nkv: int, cache_dtype: str = "bf16"):
+    """The prompt's causal attention (the HF talker's SDPA prefill, qwen3/fast.py:251-263) as a run of
+    decode steps: token t at position pos0 + t appends its k/v and attends over rows [0, pos0 + t] —
+    causal attention over the same cache, by construction. Mutates Kc/Vc; returns float64 (T, nq*hd)."""
+    rows = np.asarray(qkv_rows)
+    return np.stack([decode_step(rows[t], qn, kn, eps, rope, Kc, Vc, pos0 + t, nq, nkv, cache_dtype)
+                     for t in range(rows.shape[0])])
+
+
 def decode_step_f32(qkv, qn, kn, eps, rope, Kc, Vc, pos: int, nq: int, nkv: int, cache_dtype: str = "bf16"):
     """Same step in float32 arithmetic (numpy), used as the timed CPU port baseline."""
     hd = Kc.shape[-1]

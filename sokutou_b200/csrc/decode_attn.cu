@@ -643,6 +643,59 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
   if (!ok && t == 0) mbar_wait(&bar, 0, err);
 }
 
+// ---- prefill producer -----------------------------------------------------------------------------
+// Qwen3 prefill (the prompt's causal attention, done by the HF talker with SDPA at
+// qwen3/fast.py:251-263): for every prompt token the q heads are RMS-normalised and rotated, and the k
+// (normalised, rotated) and v rows are appended to the cache at pos0 + token — the same per-element
+// arithmetic as the decode kernel's prologue (qwen3/kernels.py:351-380), so a cache filled here holds
+// the bits decode steps would have written. q goes to q_buf (nq, T, 128) in bf16 for the tensor-core
+// attention (the 1/sqrt(128) scale is applied there). Grid (T, nkv), 256 threads: thread (g, d) owns
+// dimension d of q head kvh·2 + g, and of k (g = 0) or v (g = 1).
+template <typename CT>
+__global__ void __launch_bounds__(256) prefill_prologue_kernel(const float* __restrict__ qkv,
+                                                                const float* __restrict__ qn,
+                                                                const float* __restrict__ kn, float eps,
+                                                                const float* __restrict__ rope, CT* __restrict__ Kc,
+                                                                CT* __restrict__ Vc, __nv_bfloat16* __restrict__ q_buf,
+                                                                int pos0, int T, int max_len, int nq, int nkv) {
+  __shared__ float red[8][2];
+  __shared__ float q_s[kG][kHD];
+  __shared__ float kn_s[kHD];
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // qkv may come from the kernel just before
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int tok = blockIdx.x, kvh = blockIdx.y;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int g = t >> 7, d = t & (kHD - 1);
+  const int pos = pos0 + tok;
+  const float* row = qkv + (size_t)tok * (nq + 2 * nkv) * kHD;
+  const float qv = row[(size_t)(kvh * kG + g) * kHD + d];
+  const float xv = row[(size_t)(nq + g * nkv) * kHD + (size_t)kvh * kHD + d];  // k (g = 0) or v (g = 1)
+  const float kv = g == 0 ? xv : 0.f;
+  const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
+  if (lane == 0) {
+    red[w][0] = sq;
+    red[w][1] = sk;
+  }
+  __syncthreads();
+  const int w0 = g * 4;  // the 4 warps of this head
+  const float ssq = red[w0][0] + red[w0 + 1][0] + red[w0 + 2][0] + red[w0 + 3][0];
+  const float ssk = red[0][1] + red[1][1] + red[2][1] + red[3][1];
+  q_s[g][d] = qv * rsqrtf(ssq / kHD + eps) * qn[d];
+  if (g == 0) kn_s[d] = kv * rsqrtf(ssk / kHD + eps) * kn[d];
+  __syncthreads();
+  const float c = rope[(size_t)pos * kHD + (d & 63)];
+  const float s = rope[(size_t)pos * kHD + 64 + (d & 63)];
+  const float rot = d < 64 ? -q_s[g][d + 64] : q_s[g][d - 64];
+  q_buf[((size_t)(kvh * kG + g) * T + tok) * kHD + d] = __float2bfloat16_rn(q_s[g][d] * c + rot * s);
+  const size_t at = ((size_t)kvh * max_len + pos) * kHD + d;
+  if (g == 0) {
+    const float rk = d < 64 ? -kn_s[d + 64] : kn_s[d - 64];
+    Kc[at] = Cache<CT>::st(kn_s[d] * c + rk * s);  // qwen3/kernels.py:364,366
+  } else {
+    Vc[at] = Cache<CT>::st(xv);
+  }
+}
+
 }  // namespace decode
 }  // namespace sk
 
@@ -861,4 +914,31 @@ extern "C" int sk_decode_attention_noalloc(const float* qkv, const float* qn, co
   void* base = counters - partial_bytes;  // ws_carve(base) puts the counters exactly at `counters`
   return sk_decode_attention(qkv, qn, kn, eps, rope, Kc, Vc, pos_ptr, pos_add, max_len, nq, nkv, hd, out, base,
                              partial_bytes + (size_t)nkv * 4 + 256, cache_dtype, stream);
+}
+
+// The prefill producer launch (used by sk_prefill_attention).
+int sk_launch_prefill_prologue(const float* qkv, const float* qn, const float* kn, float eps, const float* rope,
+                               void* Kc, void* Vc, void* q_buf, int pos0, int T, int max_len, int nq, int nkv,
+                               int cache_dtype, cudaStream_t st) {
+  using namespace sk::decode;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(T, nkv);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto* qb = reinterpret_cast<__nv_bfloat16*>(q_buf);
+  const cudaError_t e =
+      cache_dtype == SK_BF16
+          ? cudaLaunchKernelEx(&cfg, prefill_prologue_kernel<__nv_bfloat16>, qkv, qn, kn, eps, rope,
+                               reinterpret_cast<__nv_bfloat16*>(Kc), reinterpret_cast<__nv_bfloat16*>(Vc), qb, pos0, T,
+                               max_len, nq, nkv)
+          : cudaLaunchKernelEx(&cfg, prefill_prologue_kernel<float>, qkv, qn, kn, eps, rope,
+                               reinterpret_cast<float*>(Kc), reinterpret_cast<float*>(Vc), qb, pos0, T, max_len, nq,
+                               nkv);
+  if (e != cudaSuccess) return SK_ERR_CUDA;
+  return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }

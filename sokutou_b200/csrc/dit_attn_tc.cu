@@ -94,6 +94,8 @@ struct TcParams {
   int ctx_batched;       // 1: ctx map has a batch coordinate
   int* err;
   int D;                 // H * hd (fused block: v and gate column offsets in o4)
+  int kv_group;          // query heads per key/value head (1 for the DiT; 2 for the Qwen3 GQA prefill)
+  int q_pos0;            // causal form: absolute position of query row 0 (key j is visible to row p if j <= p)
 };
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -168,7 +170,9 @@ __device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloa
 // FUSED = true: the attention of a DiT layer's fused block — the epilogue reads the gate tile from the
 // projection rows o4 (B·L, 4·D) through tmG and writes y · sigmoid(gate). VO4 = true: the latent v
 // tiles also come straight from o4 (tmV over o4) instead of the producer's (B, H, L, hd) buffer.
-template <int HD, bool FUSED, bool VO4>
+// CAUSAL = true: key j is visible to query row p only if j <= q_pos0 + p (the Qwen3 prefill); key tiles
+// past the CTA's last row are skipped, and the tiles that straddle the diagonal are masked per element.
+template <int HD, bool FUSED, bool VO4, bool CAUSAL>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
@@ -202,7 +206,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kBM;
-  const int n_lat = (prm.Lk + kBN - 1) / kBN, n_ctx = (prm.S + kBN - 1) / kBN;
+  const int n_lat_all = (prm.Lk + kBN - 1) / kBN, n_ctx = (prm.S + kBN - 1) / kBN;
+  // causal: only the latent key tiles up to this CTA's last query row
+  const int n_lat = CAUSAL ? min(n_lat_all, (prm.q_pos0 + q0 + kBM - 1) / kBN + 1) : n_lat_all;
   const int ntiles = n_lat + n_ctx;
 
   if (threadIdx.x == 0) {
@@ -259,7 +265,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const int bc = prm.ctx_batched ? b : 0;
       // latent tiles: (column, row, batch·head) of (B·H, L, hd) buffers; the fused block's v (and gate)
       // tiles are (column, row, batch) of o4 at column offset 2·D (3·D) plus the head's h·hd
-      const int lz = b * prm.H + h, lzv = VO4 ? b : lz;
+      // q: (b, h); k and v: the (b, h / kv_group) head of the key/value buffers
+      const int lz = b * prm.H + h, lzk = b * (prm.H / prm.kv_group) + h / prm.kv_group, lzv = VO4 ? b : lzk;
       const int xv = VO4 ? 2 * prm.D + h * HD : 0;
       mbar_arrive_expect_tx(q_full, Ly::Q_BYTES);
 #pragma unroll
@@ -282,7 +289,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           if (jk < n_lat) {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, jk * kBN, lz);
+              tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, jk * kBN, lzk);
           } else {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
@@ -422,6 +429,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[wg]);
+      if (CAUSAL && j < n_lat && (j + 1) * kBN - 1 > prm.q_pos0 + q0) {
+        // a tile straddling the diagonal: keys past this row's position are invisible
+        const int lim = prm.q_pos0 + q0 + row - j * kBN;
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) x[c] = c > lim ? -INFINITY : x[c];
+      }
       // t = s·scale·log2e + bias·log2e, packed two at a time; row max over four independent chains
       float mt0 = -INFINITY, mt1 = -INFINITY, mt2 = -INFINITY, mt3 = -INFINITY;
       const float4* bt4 = reinterpret_cast<const float4*>(bt);
@@ -629,9 +642,11 @@ static bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_
 
 // q (B, H, L, hd), k_lat (B, H, Lk, hd); v_lat (B, H, Lk, hd), or with VO4 the projection rows o4;
 // o4 (B·L, 4·D): the gate source of the fused block (unused otherwise).
-template <int HD, bool FUSED, bool VO4>
+// kv_rows: rows per head in the key/value buffers (Lk for the DiT; the cache's max_len for the prefill).
+template <int HD, bool FUSED, bool VO4, bool CAUSAL = false>
 static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const void* k_ctx, const void* v_ctx,
-                     const void* o4, long long ctx_bs, const TcParams& prm, int B, cudaStream_t st) {
+                     const void* o4, long long ctx_bs, const TcParams& prm, int B, cudaStream_t st,
+                     int kv_rows = -1) {
   using Ly = TcLayout<HD>;
   const int H = prm.H, L = prm.L, Lk = prm.Lk, S = prm.S;
   CUtensorMap mq, mk, mv, mkc, mvc;
@@ -642,8 +657,10 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     if (!make_map(&mq, q, 3, dims, str, box)) return SK_ERR_CUDA;
   }
   if (Lk > 0) {
-    cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)Lk, (cuuint64_t)B * H};
-    cuuint64_t str[2] = {(cuuint64_t)HD * 2, (cuuint64_t)Lk * HD * 2};
+    // key/value heads: H / kv_group of them per batch row, kv_rows rows apart
+    const long long rows = kv_rows > 0 ? kv_rows : Lk;
+    cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)Lk, (cuuint64_t)B * (H / prm.kv_group)};
+    cuuint64_t str[2] = {(cuuint64_t)HD * 2, (cuuint64_t)rows * HD * 2};
     cuuint32_t box[3] = {64, kBN, 1};
     if (!make_map(&mk, k_lat, 3, dims, str, box)) return SK_ERR_CUDA;
     if (!VO4 && !make_map(&mv, v_lat, 3, dims, str, box)) return SK_ERR_CUDA;
@@ -685,7 +702,7 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(attn_tc_kernel<HD, FUSED, VO4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+    if (cudaFuncSetAttribute(attn_tc_kernel<HD, FUSED, VO4, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return SK_ERR_CUDA;
     attr_done[dev] = true;
@@ -700,7 +717,8 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = sk::kUsePdl ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<HD, FUSED, VO4>, mq, mk, mv, mkc, mvc, my, mg, prm) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<HD, FUSED, VO4, CAUSAL>, mq, mk, mv, mkc, mvc, my, mg, prm) !=
+      cudaSuccess)
     return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }
@@ -743,7 +761,7 @@ extern "C" int sk_dit_attention(const void* q, const void* k_lat, const void* v_
                                        bias_batch_stride, sc, st);
   int* err = sk_error_word_ptr();
   if (!err) return SK_ERR_CUDA;
-  TcParams prm{key_bias, bias_batch_stride, y, H, L, Lk, S, sc * kLog2e, ctx_batch_stride != 0 ? 1 : 0, err, H * hd};
+  TcParams prm{key_bias, bias_batch_stride, y, H, L, Lk, S, sc * kLog2e, ctx_batch_stride != 0 ? 1 : 0, err, H * hd, 1, 0};
   return hd == 64 ? launch_tc<64, false, false>(q, k_lat, v_lat, k_ctx, v_ctx, nullptr, ctx_batch_stride, prm, B, st)
                   : launch_tc<128, false, false>(q, k_lat, v_lat, k_ctx, v_ctx, nullptr, ctx_batch_stride, prm, B, st);
 }
@@ -775,7 +793,7 @@ extern "C" int sk_dit_attention_layer(const void* o4, const float* qk_w, const f
   if (!err) return SK_ERR_CUDA;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)hd);
-  TcParams prm{key_bias, bias_batch_stride, out, H, L, L, S, sc * kLog2e, ctx_batch_stride != 0 ? 1 : 0, err, H * hd};
+  TcParams prm{key_bias, bias_batch_stride, out, H, L, L, S, sc * kLog2e, ctx_batch_stride != 0 ? 1 : 0, err, H * hd, 1, 0};
   if (hd == 64) {
     // two launches: q and k (normalised, rotated) into the caller's buffers; the attention reads v
     // and the gate straight from o4 and writes y · sigmoid(gate)
@@ -790,4 +808,33 @@ extern "C" int sk_dit_attention_layer(const void* o4, const float* qk_w, const f
   rc = launch_tc<128, false, false>(q_buf, k_buf, v_buf, k_ctx, v_ctx, nullptr, ctx_batch_stride, prm, B, st);
   if (rc != SK_OK) return rc;
   return sk_dit_gate(out, o4, out, (long long)B * L, H * hd, SK_BF16, SK_BF16, 1.f, stream);
+}
+
+int sk_launch_prefill_prologue(const float* qkv, const float* qn, const float* kn, float eps, const float* rope,
+                               void* Kc, void* Vc, void* q_buf, int pos0, int T, int max_len, int nq, int nkv,
+                               int cache_dtype, cudaStream_t st);
+
+extern "C" int sk_prefill_attention(const float* qkv, const float* qn, const float* kn, float eps, const float* rope,
+                                    void* Kc, void* Vc, int pos0, int T, int max_len, int nq, int nkv, int hd,
+                                    void* out, void* q_buf, int cache_dtype, void* stream) {
+  using namespace sk::dit;
+  if (!qkv || !qn || !kn || !rope || !Kc || !Vc || !out || !q_buf) return SK_ERR_INVALID_ARG;
+  if (T <= 0 || pos0 < 0 || max_len <= 0 || nkv <= 0 || nq <= 0 || pos0 + T > max_len) return SK_ERR_INVALID_ARG;
+  if (hd != 128 || nq != 2 * nkv) return SK_ERR_UNSUPPORTED;  // qwen3/kernels.py:457
+  if (cache_dtype != SK_BF16) return SK_ERR_UNSUPPORTED;       // the tensor-core attention needs a bf16 cache
+  if ((reinterpret_cast<uintptr_t>(Kc) | reinterpret_cast<uintptr_t>(Vc) | reinterpret_cast<uintptr_t>(out) |
+       reinterpret_cast<uintptr_t>(q_buf)) & 15)
+    return SK_ERR_INVALID_ARG;
+  int rc = sk_check_device();
+  if (rc != SK_OK) return rc;
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = sk_launch_prefill_prologue(qkv, qn, kn, eps, rope, Kc, Vc, q_buf, pos0, T, max_len, nq, nkv, cache_dtype, st);
+  if (rc != SK_OK) return rc;
+  // queries (1, nq, T, 128) from q_buf, keys and values rows [0, pos0 + T) of the cache heads
+  // (nkv, max_len, 128), query head h on key/value head h / 2, causal from row 0 at position pos0
+  const float sc = 1.0f / sqrtf(128.f);
+  TcParams prm{nullptr, 0, out, nq, T, pos0 + T, 0, sc * kLog2e, 0, err, nq * hd, nq / nkv, pos0};
+  return launch_tc<128, false, false, true>(q_buf, Kc, Vc, nullptr, nullptr, nullptr, 0, prm, 1, st, max_len);
 }

@@ -9,6 +9,7 @@ DiT (engine/fused.py:293-298):
     dit_attention_layer — the whole block (producer, attention, gate) in two launches, bf16
 Qwen3 talker (qwen3/kernels.py:622-624):
     decode_attention  — one layer's decode step with the reference kernel's argument list
+    prefill_attention — the prompt's causal attention (qwen3/fast.py:251-263), tensor cores
 """
 
 from __future__ import annotations
@@ -263,6 +264,33 @@ def decode_attention(qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps:
                                        _ptr(out), _ptr(workspace), ws_n, _dtype_code(Kc.dtype),
                                        _lib.SK_DECODE_KV_STABLE if kv_stable else 0, _stream()),
           "sk_decode_attention")
+    return out
+
+
+def prefill_attention(qkv_rows: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps: float, rope: torch.Tensor,
+                      Kc: torch.Tensor, Vc: torch.Tensor, pos0: int, max_len: int, nq: int, nkv: int,
+                      out: torch.Tensor | None = None, q_buf: torch.Tensor | None = None) -> torch.Tensor:
+    """The prompt's causal attention for one talker layer (the HF SDPA prefill, qwen3/fast.py:251-263):
+    qkv_rows float32 (T, (nq + 2*nkv)*128), one row per prompt token at positions pos0..pos0+T-1;
+    appends k/v to the bf16 caches and returns (T, nq*128) bf16."""
+    hd = Kc.shape[-1]
+    for n, t in (("qkv_rows", qkv_rows), ("qn", qn), ("kn", kn), ("rope", rope), ("Kc", Kc), ("Vc", Vc)):
+        _cuda_contig(n, t)
+    T = qkv_rows.shape[0]
+    _need(qkv_rows.dtype == torch.float32 and qkv_rows.shape == (T, (nq + 2 * nkv) * hd),
+          "qkv_rows must be float32 (T, (nq+2nkv)*hd)")
+    _need(Kc.dtype == torch.bfloat16 and Vc.dtype == torch.bfloat16, "the prefill needs bf16 caches")
+    if out is None:
+        out = torch.empty((T, nq * hd), device=Kc.device, dtype=torch.bfloat16)
+    if q_buf is None:
+        q_buf = torch.empty((nq, T, hd), device=Kc.device, dtype=torch.bfloat16)
+    _cuda_contig("out", out)
+    _cuda_contig("q_buf", q_buf)
+    _need(out.numel() == T * nq * hd and out.dtype == torch.bfloat16, "out must hold T*nq*hd bfloat16")
+    _need(q_buf.numel() >= nq * T * hd and q_buf.dtype == torch.bfloat16, "q_buf must hold nq*T*hd bfloat16")
+    check(lib().sk_prefill_attention(_ptr(qkv_rows), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
+                                     int(pos0), int(T), int(max_len), int(nq), int(nkv), int(hd), _ptr(out),
+                                     _ptr(q_buf), _dtype_code(Kc.dtype), _stream()), "sk_prefill_attention")
     return out
 
 
