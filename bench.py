@@ -484,6 +484,52 @@ def layer_block(device, dist: Dist, calls: int = 120, sets: int = 4) -> dict:
     return out
 
 
+# ------------------------------------------------------------------------------------------- prefill
+def prefill_bench(device, dist: Dist) -> dict:
+    """The c3 prompt (and a 160-token one) through all 28 talker layers' prefill attention, graph-replayed,
+    against the same tokens as decode steps (what the cache fill costs without a prefill kernel)."""
+    from sokutou_b200 import ops, qwen3, workloads as W
+    s = W.C3
+    out = {}
+    for T in (s.prompt, 160):
+        g = torch.Generator(device=device).manual_seed(T)
+        ta = qwen3.TalkerAttention(s.n_layers, s.nq, s.nkv, 1536, s.theta, s.eps, device, torch.bfloat16)
+        rows = torch.randn(s.n_layers, T, (s.nq + 2 * s.nkv) * s.hd, device=device, generator=g)
+        qn = 1 + 0.02 * torch.randn(s.n_layers, s.hd, device=device, generator=g)
+        yo = torch.empty(T, s.nq * s.hd, device=device, dtype=torch.bfloat16)
+        qb = torch.empty(s.nq, T, s.hd, device=device, dtype=torch.bfloat16)
+        od = torch.empty(s.nq * s.hd, device=device)
+
+        def run_prefill():
+            for li in range(s.n_layers):
+                ops.prefill_attention(rows[li], qn[li], qn[li], s.eps, ta.rope, ta.k[li], ta.v[li], 0, 1536, s.nq,
+                                      s.nkv, out=yo, q_buf=qb)
+
+        def run_decode():
+            for t in range(T):
+                for li in range(s.n_layers):
+                    ta.attn(li, rows[li, t], qn[li], qn[li], od, pos_add=t)
+
+        res = {}
+        for name, fn in (("prefill", run_prefill), ("decode_steps", run_decode)):
+            st = torch.cuda.Stream(device)
+            st.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(st):
+                fn()
+            torch.cuda.current_stream(device).wait_stream(st)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                fn()
+            ms = time_graphs([gr], 3, 3, dist)
+            res[f"{name}_us_per_prompt"] = round(ms * 1e3 / 3, 2)
+            del gr
+        res["layers"] = s.n_layers
+        res["speedup"] = round(res["decode_steps_us_per_prompt"] / res["prefill_us_per_prompt"], 2)
+        out[f"T{T}"] = res
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------------------------- serving
 def serving(dist: Dist, device):
     """64 requests, longest-first static sharding over the ranks; sentences/s."""
@@ -595,8 +641,9 @@ def main():
     del dec
     torch.cuda.empty_cache()
 
-    # ---- fused attention block vs its three launches
+    # ---- fused attention block vs its three launches; Qwen3 prompt prefill
     blocks = layer_block(dev, dist)
+    prefill = prefill_bench(dev, dist)
 
     # ---- c4 serving
     serv = None if a.no_serving else serving(dist, dev)
@@ -628,7 +675,7 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": UNIT,
                          "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} bf16 burst",
                          "frac_of_spec": round(achieved / SPEC["bf16_tflops"], 4), "traffic": traffic},
-            "c2": c2_res, "c3": c3_res, "layer_block": blocks, "serving": serv, "cpu_baseline": cpu,
+            "c2": c2_res, "c3": c3_res, "layer_block": blocks, "prefill": prefill, "serving": serv, "cpu_baseline": cpu,
             "clocks": clk.summary(), "device_error": err,
         }
         print(json.dumps(line), flush=True)

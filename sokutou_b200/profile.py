@@ -30,6 +30,7 @@ CASES = {
     # the block's two HBM-bound kernels alone
     "prologue_c1_L512_b3": ("prologue", W.c1(512), 3), "prologue_c2_b3": ("prologue", W.C2, 3),
     "gate_c1_L512_b3": ("gate", W.c1(512), 3), "gate_c2_b3": ("gate", W.C2, 3),
+    "prefill_T96": ("prefill", 96, None), "prefill_T160": ("prefill", 160, None),
     "decode_T128": ("decode", 128, None), "decode_T512": ("decode", 512, None),
     "decode_T1120": ("decode", 1120, None), "decode_T1500": ("decode", 1500, None),
     "decode_T1120_kvstable": ("decode", 1120, "kv_stable"), "decode_T128_kvstable": ("decode", 128, "kv_stable"),
@@ -89,6 +90,23 @@ def elementwise_case(kind, shape, B, sets, dev):
     return fns, moved, "byte"
 
 
+def prefill_case(T, sets, dev):
+    """One talker layer's prompt prefill (T tokens from position 0); work = the causal FLOPs."""
+    s = W.C3
+    max_len = 1536
+    g = torch.Generator(device=dev).manual_seed(0)
+    fns = []
+    for _ in range(sets):
+        ta = qwen3.TalkerAttention(1, s.nq, s.nkv, max_len, s.theta, s.eps, dev, torch.bfloat16)
+        rows = torch.randn(T, (s.nq + 2 * s.nkv) * s.hd, device=dev, generator=g)
+        qn = torch.ones(s.hd, device=dev)
+        out = torch.empty(T, s.nq * s.hd, device=dev, dtype=torch.bfloat16)
+        qb = torch.empty(s.nq, T, s.hd, device=dev, dtype=torch.bfloat16)
+        fns.append(lambda ta=ta, rows=rows, qn=qn, out=out, qb=qb: ops.prefill_attention(
+            rows, qn, qn, s.eps, ta.rope, ta.k[0], ta.v[0], 0, max_len, s.nq, s.nkv, out=out, q_buf=qb))
+    return fns, 4 * s.nq * s.hd * T * (T + 1) // 2, "flop"
+
+
 def decode_case(T, sets, dev, kv_stable=False):
     s = W.C3
     max_len = 1536
@@ -134,6 +152,8 @@ def main():
         fns, work, unit = elementwise_case(kind, x, B, a.sets, dev)
     elif kind in ("layer", "layer_sep"):
         fns, work, unit = layer_case(x, B, a.sets, dev, fused=(kind == "layer"))
+    elif kind == "prefill":
+        fns, work, unit = prefill_case(x, a.sets, dev)
     elif kind == "decode":
         fns, work, unit = decode_case(x, a.sets, dev, kv_stable=(B == "kv_stable"))
     else:
