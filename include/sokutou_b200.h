@@ -51,6 +51,7 @@ extern "C" {
 #define SK_DEVERR_NONE 0
 #define SK_DEVERR_POS_RANGE 1     /* decode: pos_ptr[0] + pos_add outside [0, max_len) */
 #define SK_DEVERR_TIMEOUT 2       /* a bounded mbarrier wait ran out */
+#define SK_DEVERR_BOUNDS 3        /* bounds-checked build only: an index outside its buffer (access skipped) */
 
 /* ---- dtypes ---------------------------------------------------------------------------------- */
 #define SK_BF16 0

@@ -537,7 +537,8 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj) {
         const int j = base + 8 * w + jj;
-        const float4 k4 = (ok && j < n_ld) ? Vec4<CT>::ld(Ks + (size_t)j * kHD + 4 * lane) : knew4;
+        const float4 k4 = (ok && j < n_ld && SK_INB(j < chunk_max, err)) ? Vec4<CT>::ld(Ks + (size_t)j * kHD + 4 * lane)
+                                                                          : knew4;
 #pragma unroll
         for (int g = 0; g < kG; ++g)
           part[g * 8 + jj] = qa[g].x * k4.x + qa[g].y * k4.y + qa[g].z * k4.z + qa[g].w * k4.w;
@@ -556,7 +557,7 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
       part[0] += __shfl_xor_sync(0xffffffffu, part[0], 1);
       // lane l now holds value index (l >> 1): head (l >> 4), key (l >> 1) & 7
       const int g = lane >> 4, j = base + 8 * w + ((lane >> 1) & 7);
-      if ((lane & 1) == 0 && j < n) sc[j * kG + g] = part[0];
+      if ((lane & 1) == 0 && j < n && SK_INB(j < ((chunk_max + 63) & ~63), err)) sc[j * kG + g] = part[0];
     }
   }
   __syncthreads();
@@ -609,8 +610,10 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
     float v = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) v += o_red[i][g_t][d];
-    st_async(mapa(&all_o[rank][g_t][d], 0), v, rbar);
-    if (t < kG * 2) st_async(mapa(&all_ml[rank][t >> 1][t & 1], 0), stat[t >> 1][t & 1], rbar);
+    if (SK_INB(rank < kMaxCluster, err)) {
+      st_async(mapa(&all_o[rank][g_t][d], 0), v, rbar);
+      if (t < kG * 2) st_async(mapa(&all_ml[rank][t >> 1][t & 1], 0), stat[t >> 1][t & 1], rbar);
+    }
   }
   if (rank == 0) {
     // block-uniform: a time-out seen by any thread skips the merge for the whole CTA
@@ -637,7 +640,7 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
 #pragma unroll
       for (int r = 0; r < kMaxCluster; ++r)
         if (r < CL) num += wts[r][g_t] * all_o[r][g_t][d];
-      out[(size_t)(kvh * kG + g_t) * kHD + d] = num / den_s[g_t];
+      if (SK_INB(kvh * kG + g_t < nq, err)) out[(size_t)(kvh * kG + g_t) * kHD + d] = num / den_s[g_t];
     }
   }
   if (!ok && t == 0) mbar_wait(&bar, 0, err);
@@ -657,7 +660,8 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const float* __re
                                                                 const float* __restrict__ kn, float eps,
                                                                 const float* __restrict__ rope, CT* __restrict__ Kc,
                                                                 CT* __restrict__ Vc, __nv_bfloat16* __restrict__ q_buf,
-                                                                int pos0, int T, int max_len, int nq, int nkv) {
+                                                                int pos0, int T, int max_len, int nq, int nkv,
+                                                                int* err) {
   __shared__ float red[8][2];
   __shared__ float q_s[kG][kHD];
   __shared__ float kn_s[kHD];
@@ -686,7 +690,9 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const float* __re
   const float c = rope[(size_t)pos * kHD + (d & 63)];
   const float s = rope[(size_t)pos * kHD + 64 + (d & 63)];
   const float rot = d < 64 ? -q_s[g][d + 64] : q_s[g][d - 64];
-  q_buf[((size_t)(kvh * kG + g) * T + tok) * kHD + d] = __float2bfloat16_rn(q_s[g][d] * c + rot * s);
+  if (SK_INB(kvh * kG + g < nq && tok < T, err))
+    q_buf[((size_t)(kvh * kG + g) * T + tok) * kHD + d] = __float2bfloat16_rn(q_s[g][d] * c + rot * s);
+  if (!SK_INB(pos < max_len && kvh < nkv, err)) return;
   const size_t at = ((size_t)kvh * max_len + pos) * kHD + d;
   if (g == 0) {
     const float rk = d < 64 ? -kn_s[d + 64] : kn_s[d - 64];
@@ -931,14 +937,16 @@ int sk_launch_prefill_prologue(const float* qkv, const float* qn, const float* k
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   auto* qb = reinterpret_cast<__nv_bfloat16*>(q_buf);
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
   const cudaError_t e =
       cache_dtype == SK_BF16
           ? cudaLaunchKernelEx(&cfg, prefill_prologue_kernel<__nv_bfloat16>, qkv, qn, kn, eps, rope,
                                reinterpret_cast<__nv_bfloat16*>(Kc), reinterpret_cast<__nv_bfloat16*>(Vc), qb, pos0, T,
-                               max_len, nq, nkv)
+                               max_len, nq, nkv, err)
           : cudaLaunchKernelEx(&cfg, prefill_prologue_kernel<float>, qkv, qn, kn, eps, rope,
                                reinterpret_cast<float*>(Kc), reinterpret_cast<float*>(Vc), qb, pos0, T, max_len, nq,
-                               nkv);
+                               nkv, err);
   if (e != cudaSuccess) return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }

@@ -21,7 +21,8 @@ struct KeySrc {
 template <int HD>
 __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__ q, KeySrc ks, KeySrc vs,
                                                         const float* __restrict__ bias, long long bias_bs,
-                                                        float* __restrict__ y, int H, int L, float scale) {
+                                                        float* __restrict__ y, int H, int L, float scale,
+                                                        int* err) {
   constexpr int BQ = 32, BK = 32, NC = HD / 16;  // NC float4 chunks per thread
   __shared__ __align__(16) float Ks[BK][HD];
   __shared__ __align__(16) float Vs[BK][HD];
@@ -45,6 +46,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
     for (int idx = t; idx < BK * HD / 4; idx += 128) {
       const int r = idx / (HD / 4), c4 = idx % (HD / 4), kk = k0 + r;
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (!SK_INB(r < BK && c4 < HD / 4 && b < (int)gridDim.z && h < H, err)) continue;
       if (kk < ks.Lk) {
         const size_t off = (((size_t)b * H + h) * ks.Lk + kk) * HD;
         kv = reinterpret_cast<const float4*>(ks.lat + off)[c4];
@@ -59,7 +61,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
     }
     if (t < BK) {
       const int kk = k0 + t;
-      bs[t] = (kk >= K) ? -INFINITY : (bias ? bias[(size_t)b * bias_bs + kk] : 0.f);
+      bs[t] = (kk >= K || !SK_INB(kk >= 0, err)) ? -INFINITY : (bias ? bias[(size_t)b * bias_bs + kk] : 0.f);
     }
     __syncthreads();
     float s[BK];
@@ -106,7 +108,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
     }
     m = m_new;
   }
-  if (qi < L) {
+  if (qi < L && SK_INB(qi >= 0 && h < H, err)) {
     const float inv = (l > 0.f) ? 1.f / l : 0.f;
     float4* yo = reinterpret_cast<float4*>(y + (((size_t)b * L + qi) * H + h) * HD);
 #pragma unroll
@@ -122,10 +124,12 @@ int sk_launch_dit_attention_f32(const float* q, const float* k_lat, const float*
                                 int hd, long long ctx_bs, long long bias_bs, float scale, cudaStream_t st) {
   using namespace sk::dit;
   KeySrc ks{k_lat, k_ctx, ctx_bs, Lk, S}, vs{v_lat, v_ctx, ctx_bs, Lk, S};
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
   dim3 grid((L + 31) / 32, H, B), block(128);
   if (hd == 64)
-    attn_f32_kernel<64><<<grid, block, 0, st>>>(q, ks, vs, bias, bias_bs, y, H, L, scale);
+    attn_f32_kernel<64><<<grid, block, 0, st>>>(q, ks, vs, bias, bias_bs, y, H, L, scale, err);
   else
-    attn_f32_kernel<128><<<grid, block, 0, st>>>(q, ks, vs, bias, bias_bs, y, H, L, scale);
+    attn_f32_kernel<128><<<grid, block, 0, st>>>(q, ks, vs, bias, bias_bs, y, H, L, scale, err);
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }

@@ -163,6 +163,7 @@ __device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloa
     key = kk < prm.S ? prm.Lk + kk : -1;
   }
   if (key < 0) return -INFINITY;
+  if (!SK_INB(key < prm.Lk + prm.S && b < (int)gridDim.z, prm.err)) return 0.f;
   return bias ? __bfloat162float(bias[(size_t)b * prm.bias_bs + key]) * kLog2e : 0.f;
 }
 
@@ -415,7 +416,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     for (int j = wg; j < ntiles && ok; j += 2) {
       const int it = j >> 1;  // this warpgroup's tile count so far
       float* bt = bias_s + (wg * 2 + (it & 1)) * kBN;
-      bt[row] = bnext;
+      if (SK_INB(row < kBN && wg * 2 + (it & 1) < 4, prm.err)) bt[row] = bnext;
       if (j + 2 < ntiles) bnext = tile_bias(prm, bias, b, j + 2, n_lat, row);  // lands during this tile
       named_bar_sync(1 + wg, 128);
       if (!mbar_wait(&s_full[wg], it & 1, prm.err)) {
@@ -514,8 +515,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           pk[e] = *reinterpret_cast<const uint32_t*>(&pb2);
         }
         const int chunk = u >> 3, unit = u & 7;
-        *reinterpret_cast<uint4*>(prow + chunk * (kBM * 128) + ((unit ^ (row & 7)) << 4)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        const int poff = chunk * (kBM * 128) + row * 128 + ((unit ^ (row & 7)) << 4);  // within this group's P tile
+        if (SK_INB(poff + 16 <= Ly::P_BYTES, prm.err))
+          *reinterpret_cast<uint4*>(prow + chunk * (kBM * 128) + ((unit ^ (row & 7)) << 4)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l_run += (ls0.x + ls0.y) + (ls1.x + ls1.y);
       fence_proxy_async_smem();
@@ -526,8 +529,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     named_bar_sync(1 + wg, 128);  // this warpgroup is done reading its bias area
     {
       float* ml = bias_s + wg * 2 * kBN;  // [kBM][2]
-      ml[row * 2] = m_run;
-      ml[row * 2 + 1] = l_run;
+      if (SK_INB(row * 2 + 1 < 2 * kBN, prm.err)) {
+        ml[row * 2] = m_run;
+        ml[row * 2 + 1] = l_run;
+      }
     }
     named_bar_sync(3, 256);
     bool okk = ok;
@@ -567,9 +572,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           uint32_t pk[4];
           const int unit = ((col & 63) >> 3) + u;
           uint32_t gw[4] = {0, 0, 0, 0};
-          if (FUSED) {  // the gate tile sits where Q was, in the same swizzled layout
-            const uint4 g4 = *reinterpret_cast<const uint4*>(smem + Ly::OFF_Q + (col >> 6) * (kBM * 128) + row * 128 +
-                                                             ((unit ^ (row & 7)) << 4));
+          const int goff = (col >> 6) * (kBM * 128) + row * 128 + ((unit ^ (row & 7)) << 4);
+          if (FUSED && SK_INB(goff + 16 <= Ly::Q_BYTES, prm.err)) {  // the gate tile sits where Q was, same layout
+            const uint4 g4 = *reinterpret_cast<const uint4*>(smem + Ly::OFF_Q + goff);
             gw[0] = g4.x, gw[1] = g4.y, gw[2] = g4.z, gw[3] = g4.w;
           }
 #pragma unroll
@@ -589,9 +594,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             const __nv_bfloat162 v2 = __floats2bfloat162_rn(y0, y1);
             pk[e] = *reinterpret_cast<const uint32_t*>(&v2);
           }
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + ((unit ^ (row & 7)) << 4))),
-                       "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3])
-                       : "memory");
+          if (SK_INB((col >> 6) * (kBM * 128) + row * 128 + ((unit ^ (row & 7)) << 4) + 16 <= 2 * Ly::P_BYTES, prm.err))
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + ((unit ^ (row & 7)) << 4))),
+                         "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3])
+                         : "memory");
         }
       }
       fence_proxy_async_smem();

@@ -30,6 +30,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // A bounded wait gives up after this long; every legitimate wait in these kernels is microseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Bounds-checked build (-DSK_BOUNDS_CHECK=1, lib/libsokutou_b200_checked.so): every guarded shared,
+// tensor or global memory index is tested before its access; an index out of range records
+// SK_DEVERR_BOUNDS in the error word and the access is skipped (never a trap). The normal build
+// compiles the guards away.
+#ifndef SK_BOUNDS_CHECK
+#define SK_BOUNDS_CHECK 0
+#endif
+__device__ __forceinline__ bool sk_in_bounds(bool cond, int* err) {
+  if (SK_BOUNDS_CHECK && !cond) {
+    atomicCAS(err, 0, SK_DEVERR_BOUNDS);
+    return false;
+  }
+  return true;
+}
+#define SK_INB(cond, err) (!SK_BOUNDS_CHECK || sk_in_bounds((cond), (err)))
 // Programmatic dependent launch for the DiT kernels (each waits for its predecessor with
 // griddepcontrol.wait before reading global memory, so this only moves set-up earlier).
 #ifndef SK_USE_PDL

@@ -44,3 +44,14 @@ def cuda():
     from sokutou_b200 import build
     build.build()
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _no_bounds_error(request):
+    """Under SOKUTOU_B200_CHECK_BOUNDS=1 (the bounds-checked library's run), every GPU test must leave
+    no SK_DEVERR_BOUNDS in the device error word."""
+    yield
+    if os.environ.get("SOKUTOU_B200_CHECK_BOUNDS") == "1" and "gpu" in request.keywords:
+        from sokutou_b200 import ops
+        code = ops.device_error(reset=True)
+        assert code != 3, f"an index out of its buffer in {request.node.name} (SK_DEVERR_BOUNDS)"
