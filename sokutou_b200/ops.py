@@ -14,12 +14,23 @@ Qwen3 talker (qwen3/kernels.py:622-624):
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import os
 
 import torch
 
 from . import _lib
 from ._lib import SK_BF16, SK_E4M3, SK_F32, check, lib
+
+
+_NVTX = os.environ.get("SOKUTOU_B200_NVTX") == "1"
+
+
+def _nvtx(name: str):
+    """An NVTX range per op launch (SOKUTOU_B200_NVTX=1) so a profiler can select one op's kernels
+    (ncu --nvtx --nvtx-include "sk_decode_attention/"); a no-op otherwise."""
+    return torch.cuda.nvtx.range(name) if _NVTX else contextlib.nullcontext()
 
 
 def _ptr(t: torch.Tensor | None) -> int:
@@ -51,7 +62,8 @@ def _cuda_contig(name: str, t: torch.Tensor) -> None:
 def device_error(reset: bool = True) -> int:
     """The device error word of the current device (0 = none); synchronises the device."""
     code = ctypes.c_int(0)
-    check(lib().sk_device_error(ctypes.byref(code), int(reset)), "sk_device_error")
+    with _nvtx("sk_device_error"):
+        check(lib().sk_device_error(ctypes.byref(code), int(reset)), "sk_device_error")
     return code.value
 
 
@@ -75,8 +87,9 @@ def dit_qkv_prologue(o4: torch.Tensor, qk_w: torch.Tensor, freqs: torch.Tensor, 
     for n, t in (("q", q), ("k_lat", k), ("v_lat", v)):
         _cuda_contig(n, t)
         _need(t.shape == (B, H, L, hd) and t.dtype == o4.dtype, f"{n} must be ({B}, {H}, {L}, {hd}) {o4.dtype}")
-    check(lib().sk_dit_qkv_prologue(_ptr(o4), _ptr(qk_w), _ptr(freqs), _ptr(q), _ptr(k), _ptr(v), B, L, H, hd,
-                                    float(eps), _dtype_code(o4.dtype), _stream()), "sk_dit_qkv_prologue")
+    with _nvtx("sk_dit_qkv_prologue"):
+        check(lib().sk_dit_qkv_prologue(_ptr(o4), _ptr(qk_w), _ptr(freqs), _ptr(q), _ptr(k), _ptr(v), B, L, H, hd,
+                                        float(eps), _dtype_code(o4.dtype), _stream()), "sk_dit_qkv_prologue")
     return q, k, v
 
 
@@ -122,9 +135,10 @@ def dit_attention(q: torch.Tensor, k_lat: torch.Tensor, v_lat: torch.Tensor, k_c
         out = torch.empty((B, L, H, hd), device=q.device, dtype=dt)
     _cuda_contig("out", out)
     _need(out.shape == (B, L, H, hd) and out.dtype == dt, "out must be (B, L, H, hd) in q's dtype")
-    check(lib().sk_dit_attention(_ptr(q), _ptr(k_lat), _ptr(v_lat), _ptr(k_ctx), _ptr(v_ctx), _ptr(bias), _ptr(out),
-                                 B, H, L, Lk, S, hd, ctx_bs, bias_bs, _dtype_code(dt), float(scale or 0.0), _stream()),
-          "sk_dit_attention")
+    with _nvtx("sk_dit_attention"):
+        check(lib().sk_dit_attention(_ptr(q), _ptr(k_lat), _ptr(v_lat), _ptr(k_ctx), _ptr(v_ctx), _ptr(bias), _ptr(out),
+                                     B, H, L, Lk, S, hd, ctx_bs, bias_bs, _dtype_code(dt), float(scale or 0.0), _stream()),
+              "sk_dit_attention")
     return out
 
 
@@ -194,10 +208,11 @@ def dit_attention_layer(o4: torch.Tensor, qk_w: torch.Tensor, freqs: torch.Tenso
     for n, t in zip(("q_buf", "k_buf", "v_buf"), qkv_bufs):
         _cuda_contig(n, t)
         _need(t.shape == (B, H, L, hd) and t.dtype == o4.dtype, f"{n} must be ({B}, {H}, {L}, {hd}) bfloat16")
-    check(lib().sk_dit_attention_layer(_ptr(o4), _ptr(qk_w), _ptr(freqs), _ptr(k_ctx), _ptr(v_ctx), _ptr(bias),
-                                       _ptr(out), _ptr(qkv_bufs[0]), _ptr(qkv_bufs[1]), _ptr(qkv_bufs[2]), B, H, L,
-                                       S, hd, ctx_bs, bias_bs, float(eps), SK_BF16, float(scale or 0.0), _stream()),
-          "sk_dit_attention_layer")
+    with _nvtx("sk_dit_attention_layer"):
+        check(lib().sk_dit_attention_layer(_ptr(o4), _ptr(qk_w), _ptr(freqs), _ptr(k_ctx), _ptr(v_ctx), _ptr(bias),
+                                           _ptr(out), _ptr(qkv_bufs[0]), _ptr(qkv_bufs[1]), _ptr(qkv_bufs[2]), B, H, L,
+                                           S, hd, ctx_bs, bias_bs, float(eps), SK_BF16, float(scale or 0.0), _stream()),
+              "sk_dit_attention_layer")
     return out
 
 
@@ -223,8 +238,9 @@ def dit_gate(y: torch.Tensor, o4: torch.Tensor, out: torch.Tensor | None = None,
         out = torch.empty((rows, D), device=y.device, dtype=odt)
     _cuda_contig("out", out)
     _need(out.dtype == odt and out.numel() == rows * D, f"out must hold {rows}x{D} {odt}")
-    check(lib().sk_dit_gate(_ptr(y), _ptr(o4), _ptr(out), rows, D, code, out_code,
-                            float(fp8_scale if fp8_scale is not None else 1.0), _stream()), "sk_dit_gate")
+    with _nvtx("sk_dit_gate"):
+        check(lib().sk_dit_gate(_ptr(y), _ptr(o4), _ptr(out), rows, D, code, out_code,
+                                float(fp8_scale if fp8_scale is not None else 1.0), _stream()), "sk_dit_gate")
     return out
 
 
@@ -259,11 +275,12 @@ def decode_attention(qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps:
     if pos_ptr is not None:
         _need(pos_ptr.is_cuda and pos_ptr.dtype == torch.int64, "pos_ptr must be a CUDA int64 tensor")
     ws_n = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    check(lib().sk_decode_attention_ex(_ptr(qkv), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
-                                       _ptr(pos_ptr), int(pos_add), int(max_len), int(nq), int(nkv), int(hd),
-                                       _ptr(out), _ptr(workspace), ws_n, _dtype_code(Kc.dtype),
-                                       _lib.SK_DECODE_KV_STABLE if kv_stable else 0, _stream()),
-          "sk_decode_attention")
+    with _nvtx("sk_decode_attention_ex"):
+        check(lib().sk_decode_attention_ex(_ptr(qkv), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
+                                           _ptr(pos_ptr), int(pos_add), int(max_len), int(nq), int(nkv), int(hd),
+                                           _ptr(out), _ptr(workspace), ws_n, _dtype_code(Kc.dtype),
+                                           _lib.SK_DECODE_KV_STABLE if kv_stable else 0, _stream()),
+              "sk_decode_attention")
     return out
 
 
@@ -288,9 +305,10 @@ def prefill_attention(qkv_rows: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor
     _cuda_contig("q_buf", q_buf)
     _need(out.numel() == T * nq * hd and out.dtype == torch.bfloat16, "out must hold T*nq*hd bfloat16")
     _need(q_buf.numel() >= nq * T * hd and q_buf.dtype == torch.bfloat16, "q_buf must hold nq*T*hd bfloat16")
-    check(lib().sk_prefill_attention(_ptr(qkv_rows), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
-                                     int(pos0), int(T), int(max_len), int(nq), int(nkv), int(hd), _ptr(out),
-                                     _ptr(q_buf), _dtype_code(Kc.dtype), _stream()), "sk_prefill_attention")
+    with _nvtx("sk_prefill_attention"):
+        check(lib().sk_prefill_attention(_ptr(qkv_rows), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
+                                         int(pos0), int(T), int(max_len), int(nq), int(nkv), int(hd), _ptr(out),
+                                         _ptr(q_buf), _dtype_code(Kc.dtype), _stream()), "sk_prefill_attention")
     return out
 
 

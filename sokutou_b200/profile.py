@@ -3,8 +3,11 @@
     python -m sokutou_b200.profile --case dit_c1_L512_b3 [--reps 50] [--graph]
     python -m sokutou_b200.profile --case decode_T1120 [--reps 50] [--graph]
 
-Prints one JSON line: average microseconds per call from CUDA events over `reps` back-to-back calls
-(eager launches, or one CUDA graph holding them with --graph), and the algorithmic work per call.
+Prints one JSON record: the case's shape, average microseconds per call from CUDA events over `reps`
+back-to-back calls (eager launches, or one CUDA graph holding them with --graph), the algorithmic work
+per call, the rate and its fraction of the measured peak (MEASURED_PEAKS.json: bf16 tensor TFLOP/s
+for contractions, HBM GB/s for the rest) and, with --cpu, the same call timed on the host cores with
+torch's fp32 SDPA (the reference's own op) beside it.
 Inputs: distinct buffers per call, rotated over `--sets` copies so that a run can exceed L2.
 """
 
@@ -143,6 +146,7 @@ def main():
     ap.add_argument("--sets", type=int, default=4)
     ap.add_argument("--graph", action="store_true")
     ap.add_argument("--warm-ms", type=float, default=300.0, help="busy time before timing (clock ramp-up)")
+    ap.add_argument("--cpu", action="store_true", help="also time the call on the host CPU (DiT cases)")
     a = ap.parse_args()
     dev = torch.device("cuda:0")
     kind, x, B = CASES[a.case]
@@ -187,10 +191,57 @@ def main():
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / a.reps
     rate = work / (us * 1e-6) / (1e12 if unit == "flop" else 1e9)
-    print(json.dumps({"case": a.case, "graph": a.graph, "reps": a.reps, "us_per_call": round(us, 3),
-                      f"{unit}s_per_call": work, ("TFLOP/s" if unit == "flop" else "GB/s"): round(rate, 2),
-                      "device_error": ops.device_error()}))
+    rec = {"case": a.case, "kind": kind, "shape": _shape(kind, x, B), "graph": a.graph, "reps": a.reps,
+           "us_per_call": round(us, 3), f"{unit}s_per_call": work,
+           ("TFLOP/s" if unit == "flop" else "GB/s"): round(rate, 2)}
+    peak_key = "bf16_tflops" if unit == "flop" else "hbm_gbs"
+    peak = _peaks().get(peak_key)
+    if peak:
+        rec["frac_of_measured_peak"] = round(rate / peak, 4)
+    if a.cpu and kind in ("dit", "layer", "layer_sep"):
+        rec["cpu"] = _cpu_dit(x, B)
+    rec["device_error"] = ops.device_error()
+    print(json.dumps(rec))
 
 
-if __name__ == "__main__":
-    main()
+def _shape(kind, x, B):
+    if kind in ("dit", "layer", "layer_sep", "prologue", "gate"):
+        return {"B": B, "H": x.H, "hd": x.hd, "L": x.L, "text_keys": x.Tb, "speaker_keys": x.Sp}
+    if kind in ("decode", "prefill"):
+        s = W.C3
+        return {"T": x, "nq": s.nq, "nkv": s.nkv, "hd": s.hd}
+    return {"bytes": x}
+
+
+def _peaks() -> dict:
+    import os
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in ("bf16_tflops", "hbm_gbs") if k in d}
+    except (OSError, ValueError, KeyError):
+        return {}
+
+
+def _cpu_dit(shape, B) -> dict:
+    """The same attention call on the host CPU: torch's scaled_dot_product_attention in fp32 with all host
+    threads (the reference's own op, engine/fused.py:295, ctx keys copied per CFG row as the reference
+    does), median of 3 runs."""
+    import os
+    import time
+
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(0)
+    H, hd, L, S = shape.H, shape.hd, shape.L, shape.S
+    q = torch.randn(B, H, L, hd, generator=g)
+    k = torch.randn(B, H, L + S, hd, generator=g)
+    v = torch.randn(B, H, L + S, hd, generator=g)
+    mask = torch.zeros(B, 1, 1, L + S)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+        times.append(time.perf_counter() - t0)
+    t = sorted(times)[1]
+    return {"us_per_call": round(t * 1e6, 1), "TFLOP/s": round(shape.flops(B) / t / 1e12, 4), "cores": os.cpu_count()}
