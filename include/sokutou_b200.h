@@ -210,7 +210,8 @@ SK_API int sk_decode_attention_ex(const float* qkv, const float* qn, const float
 
 /*
  * Qwen3 prefill attention: the prompt's causal self-attention, which the reference runs inside the HF
- * talker with SDPA (qwen3/fast.py:251-263), on the tensor-core kernel with a causal mask and GQA.
+ * talker with SDPA (qwen3/fast.py:251-263): bf16 caches on the tensor-core kernel with a causal mask
+ * and GQA; fp32 caches (the fp32 parity mode) on the fp32 CUDA-core kernel with the same masking.
  * For every prompt token t in [0, T) at position pos0 + t:
  *   - q heads RMS-normalised (× qn) and rotated (rotate-half RoPE from `rope`, as sk_decode_attention),
  *     k normalised (× kn) and rotated, v raw; k and v appended to the caches at row pos0 + t (the bits
@@ -218,8 +219,8 @@ SK_API int sk_decode_attention_ex(const float* qkv, const float* qn, const float
  *   - out[t] = softmax(q·kᵀ / sqrt(128)) · v over the cache rows [0, pos0 + t] of the key/value head
  *     h / 2 (earlier rows pos0 > 0: a prompt chunk after a cached prefix).
  *   qkv   : fp32 (T, (nq + 2*nkv) * 128) rows = [q heads | k heads | v heads] per token
- *   Kc, Vc: this layer's cache [nkv][max_len][128], bf16 (cache_dtype SK_BF16 only)
- *   out   : (T, nq * 128) bf16;  q_buf: caller scratch (nq, T, 128) bf16
+ *   Kc, Vc: this layer's cache [nkv][max_len][128], bf16 (SK_BF16) or fp32 (SK_F32)
+ *   out   : (T, nq * 128) in the cache dtype;  q_buf: caller scratch (nq, T, 128) in the cache dtype
  *   hd = 128, nq = 2*nkv, pos0 + T <= max_len; buffers 16-byte aligned.
  */
 SK_API int sk_prefill_attention(const float* qkv, const float* qn, const float* kn, float eps,

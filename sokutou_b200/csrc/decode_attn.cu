@@ -651,15 +651,15 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
 // qwen3/fast.py:251-263): for every prompt token the q heads are RMS-normalised and rotated, and the k
 // (normalised, rotated) and v rows are appended to the cache at pos0 + token — the same per-element
 // arithmetic as the decode kernel's prologue (qwen3/kernels.py:351-380), so a cache filled here holds
-// the bits decode steps would have written. q goes to q_buf (nq, T, 128) in bf16 for the tensor-core
-// attention (the 1/sqrt(128) scale is applied there). Grid (T, nkv), 256 threads: thread (g, d) owns
+// the bits decode steps would have written. q goes to q_buf (nq, T, 128) in the cache dtype (bf16 for
+// the tensor-core attention, fp32 for the fp32 mode; the 1/sqrt(128) scale is applied there). Grid (T, nkv), 256 threads: thread (g, d) owns
 // dimension d of q head kvh·2 + g, and of k (g = 0) or v (g = 1).
 template <typename CT>
 __global__ void __launch_bounds__(256) prefill_prologue_kernel(const float* __restrict__ qkv,
                                                                 const float* __restrict__ qn,
                                                                 const float* __restrict__ kn, float eps,
                                                                 const float* __restrict__ rope, CT* __restrict__ Kc,
-                                                                CT* __restrict__ Vc, __nv_bfloat16* __restrict__ q_buf,
+                                                                CT* __restrict__ Vc, CT* __restrict__ q_buf,
                                                                 int pos0, int T, int max_len, int nq, int nkv,
                                                                 int* err) {
   __shared__ float red[8][2];
@@ -691,7 +691,7 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const float* __re
   const float s = rope[(size_t)pos * kHD + 64 + (d & 63)];
   const float rot = d < 64 ? -q_s[g][d + 64] : q_s[g][d - 64];
   if (SK_INB(kvh * kG + g < nq && tok < T, err))
-    q_buf[((size_t)(kvh * kG + g) * T + tok) * kHD + d] = __float2bfloat16_rn(q_s[g][d] * c + rot * s);
+    q_buf[((size_t)(kvh * kG + g) * T + tok) * kHD + d] = Cache<CT>::st(q_s[g][d] * c + rot * s);
   if (!SK_INB(pos < max_len && kvh < nkv, err)) return;
   const size_t at = ((size_t)kvh * max_len + pos) * kHD + d;
   if (g == 0) {
@@ -936,17 +936,16 @@ int sk_launch_prefill_prologue(const float* qkv, const float* qn, const float* k
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  auto* qb = reinterpret_cast<__nv_bfloat16*>(q_buf);
   int* err = sk_error_word_ptr();
   if (!err) return SK_ERR_CUDA;
   const cudaError_t e =
       cache_dtype == SK_BF16
           ? cudaLaunchKernelEx(&cfg, prefill_prologue_kernel<__nv_bfloat16>, qkv, qn, kn, eps, rope,
-                               reinterpret_cast<__nv_bfloat16*>(Kc), reinterpret_cast<__nv_bfloat16*>(Vc), qb, pos0, T,
-                               max_len, nq, nkv, err)
+                               reinterpret_cast<__nv_bfloat16*>(Kc), reinterpret_cast<__nv_bfloat16*>(Vc),
+                               reinterpret_cast<__nv_bfloat16*>(q_buf), pos0, T, max_len, nq, nkv, err)
           : cudaLaunchKernelEx(&cfg, prefill_prologue_kernel<float>, qkv, qn, kn, eps, rope,
-                               reinterpret_cast<float*>(Kc), reinterpret_cast<float*>(Vc), qb, pos0, T, max_len, nq,
-                               nkv, err);
+                               reinterpret_cast<float*>(Kc), reinterpret_cast<float*>(Vc),
+                               reinterpret_cast<float*>(q_buf), pos0, T, max_len, nq, nkv, err);
   if (e != cudaSuccess) return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }

@@ -12,10 +12,14 @@ namespace sk {
 namespace dit {
 
 struct KeySrc {
-  const float* lat;   // (B, H, Lk, HD)
+  const float* lat;   // (B, H / group, rows, HD): latent keys 0..Lk-1 of each key/value head
   const float* ctx;   // (S, H, HD) per batch row
   long long ctx_bs;   // elements between ctx batch rows (0 = shared)
   int Lk, S;
+  int group = 1;      // query heads per key/value head (2: the Qwen3 GQA prefill)
+  int rows = 0;       // rows per key/value head in `lat` (0: Lk)
+  int causal = 0;     // 1: key j visible to query row p only if j <= pos0 + p (the Qwen3 prefill)
+  int pos0 = 0;
 };
 
 template <int HD>
@@ -30,7 +34,9 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
   const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * BQ;
   const int t = threadIdx.x, row = t >> 2, quad = t & 3;
   const int qi = q0 + row;
-  const int K = ks.Lk + ks.S;
+  // causal: no key past the CTA's last query row is visible to any of its rows
+  const int K = ks.causal ? min(ks.Lk + ks.S, ks.pos0 + q0 + BQ) : ks.Lk + ks.S;
+  const int kvh = h / ks.group, kv_rows = ks.rows > 0 ? ks.rows : ks.Lk;
 
   float4 qr[NC], o[NC];
 #pragma unroll
@@ -48,7 +54,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
       if (!SK_INB(r < BK && c4 < HD / 4 && b < (int)gridDim.z && h < H, err)) continue;
       if (kk < ks.Lk) {
-        const size_t off = (((size_t)b * H + h) * ks.Lk + kk) * HD;
+        const size_t off = (((size_t)b * (H / ks.group) + kvh) * kv_rows + kk) * HD;
         kv = reinterpret_cast<const float4*>(ks.lat + off)[c4];
         vv = reinterpret_cast<const float4*>(vs.lat + off)[c4];
       } else if (kk < K) {
@@ -79,7 +85,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
       }
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      s[j] = acc * scale + bs[j];
+      s[j] = (ks.causal && k0 + j > ks.pos0 + qi) ? -INFINITY : acc * scale + bs[j];
       mt = fmaxf(mt, s[j]);
     }
     const float m_new = fmaxf(m, mt);
@@ -131,5 +137,19 @@ int sk_launch_dit_attention_f32(const float* q, const float* k_lat, const float*
     attn_f32_kernel<64><<<grid, block, 0, st>>>(q, ks, vs, bias, bias_bs, y, H, L, scale, err);
   else
     attn_f32_kernel<128><<<grid, block, 0, st>>>(q, ks, vs, bias, bias_bs, y, H, L, scale, err);
+  return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
+}
+
+// The Qwen3 prefill in the fp32 mode: q (nq, T, 128), keys/values rows [0, pos0 + T) of the cache heads
+// (nkv, max_len, 128), query head h on head h / 2, causal; y (T, nq, 128).
+int sk_launch_prefill_attention_f32(const float* q, const float* Kc, const float* Vc, float* y, int nq, int nkv,
+                                    int T, int pos0, int max_len, cudaStream_t st) {
+  using namespace sk::dit;
+  KeySrc ks{Kc, nullptr, 0, pos0 + T, 0, nq / nkv, max_len, 1, pos0};
+  KeySrc vs{Vc, nullptr, 0, pos0 + T, 0, nq / nkv, max_len, 1, pos0};
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
+  dim3 grid((T + 31) / 32, nq, 1), block(128);
+  attn_f32_kernel<128><<<grid, block, 0, st>>>(q, ks, vs, nullptr, 0, y, nq, T, 1.0f / sqrtf(128.f), err);
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }

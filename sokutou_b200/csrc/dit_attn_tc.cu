@@ -819,6 +819,8 @@ extern "C" int sk_dit_attention_layer(const void* o4, const float* qk_w, const f
 int sk_launch_prefill_prologue(const float* qkv, const float* qn, const float* kn, float eps, const float* rope,
                                void* Kc, void* Vc, void* q_buf, int pos0, int T, int max_len, int nq, int nkv,
                                int cache_dtype, cudaStream_t st);
+int sk_launch_prefill_attention_f32(const float* q, const float* Kc, const float* Vc, float* y, int nq, int nkv,
+                                    int T, int pos0, int max_len, cudaStream_t st);
 
 extern "C" int sk_prefill_attention(const float* qkv, const float* qn, const float* kn, float eps, const float* rope,
                                     void* Kc, void* Vc, int pos0, int T, int max_len, int nq, int nkv, int hd,
@@ -827,7 +829,7 @@ extern "C" int sk_prefill_attention(const float* qkv, const float* qn, const flo
   if (!qkv || !qn || !kn || !rope || !Kc || !Vc || !out || !q_buf) return SK_ERR_INVALID_ARG;
   if (T <= 0 || pos0 < 0 || max_len <= 0 || nkv <= 0 || nq <= 0 || pos0 + T > max_len) return SK_ERR_INVALID_ARG;
   if (hd != 128 || nq != 2 * nkv) return SK_ERR_UNSUPPORTED;  // qwen3/kernels.py:457
-  if (cache_dtype != SK_BF16) return SK_ERR_UNSUPPORTED;       // the tensor-core attention needs a bf16 cache
+  if (cache_dtype != SK_BF16 && cache_dtype != SK_F32) return SK_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(Kc) | reinterpret_cast<uintptr_t>(Vc) | reinterpret_cast<uintptr_t>(out) |
        reinterpret_cast<uintptr_t>(q_buf)) & 15)
     return SK_ERR_INVALID_ARG;
@@ -838,6 +840,10 @@ extern "C" int sk_prefill_attention(const float* qkv, const float* qn, const flo
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   rc = sk_launch_prefill_prologue(qkv, qn, kn, eps, rope, Kc, Vc, q_buf, pos0, T, max_len, nq, nkv, cache_dtype, st);
   if (rc != SK_OK) return rc;
+  if (cache_dtype == SK_F32)  // the fp32 mode: CUDA-core fp32 attention
+    return sk_launch_prefill_attention_f32(static_cast<const float*>(q_buf), static_cast<const float*>(Kc),
+                                           static_cast<const float*>(Vc), static_cast<float*>(out), nq, nkv, T, pos0,
+                                           max_len, st);
   // queries (1, nq, T, 128) from q_buf, keys and values rows [0, pos0 + T) of the cache heads
   // (nkv, max_len, 128), query head h on key/value head h / 2, causal from row 0 at position pos0
   const float sc = 1.0f / sqrtf(128.f);

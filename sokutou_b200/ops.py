@@ -289,22 +289,24 @@ def prefill_attention(qkv_rows: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor
                       out: torch.Tensor | None = None, q_buf: torch.Tensor | None = None) -> torch.Tensor:
     """The prompt's causal attention for one talker layer (the HF SDPA prefill, qwen3/fast.py:251-263):
     qkv_rows float32 (T, (nq + 2*nkv)*128), one row per prompt token at positions pos0..pos0+T-1;
-    appends k/v to the bf16 caches and returns (T, nq*128) bf16."""
+    appends k/v to the caches and returns (T, nq*128) in the cache dtype (bf16: tensor cores; fp32:
+    the fp32 parity mode)."""
     hd = Kc.shape[-1]
     for n, t in (("qkv_rows", qkv_rows), ("qn", qn), ("kn", kn), ("rope", rope), ("Kc", Kc), ("Vc", Vc)):
         _cuda_contig(n, t)
     T = qkv_rows.shape[0]
     _need(qkv_rows.dtype == torch.float32 and qkv_rows.shape == (T, (nq + 2 * nkv) * hd),
           "qkv_rows must be float32 (T, (nq+2nkv)*hd)")
-    _need(Kc.dtype == torch.bfloat16 and Vc.dtype == torch.bfloat16, "the prefill needs bf16 caches")
+    dt = Kc.dtype
+    _need(dt in (torch.bfloat16, torch.float32) and Vc.dtype == dt, "caches must both be bfloat16 or float32")
     if out is None:
-        out = torch.empty((T, nq * hd), device=Kc.device, dtype=torch.bfloat16)
+        out = torch.empty((T, nq * hd), device=Kc.device, dtype=dt)
     if q_buf is None:
-        q_buf = torch.empty((nq, T, hd), device=Kc.device, dtype=torch.bfloat16)
+        q_buf = torch.empty((nq, T, hd), device=Kc.device, dtype=dt)
     _cuda_contig("out", out)
     _cuda_contig("q_buf", q_buf)
-    _need(out.numel() == T * nq * hd and out.dtype == torch.bfloat16, "out must hold T*nq*hd bfloat16")
-    _need(q_buf.numel() >= nq * T * hd and q_buf.dtype == torch.bfloat16, "q_buf must hold nq*T*hd bfloat16")
+    _need(out.numel() == T * nq * hd and out.dtype == dt, f"out must hold T*nq*hd {dt}")
+    _need(q_buf.numel() >= nq * T * hd and q_buf.dtype == dt, f"q_buf must hold nq*T*hd {dt}")
     with _nvtx("sk_prefill_attention"):
         check(lib().sk_prefill_attention(_ptr(qkv_rows), _ptr(qn), _ptr(kn), float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc),
                                          int(pos0), int(T), int(max_len), int(nq), int(nkv), int(hd), _ptr(out),

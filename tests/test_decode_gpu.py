@@ -262,26 +262,28 @@ def test_kv_stable_launch_gives_same_bits(cuda, cache):
         assert torch.equal(a, b)
 
 
-def _prefill_case(d, max_len, pos0, T, seed):
+def _prefill_case(d, max_len, pos0, T, seed, cache="bf16"):
     s = W.C3
     g = torch.Generator().manual_seed(seed)
-    Kc = torch.randn(s.nkv, max_len, 128, generator=g).bfloat16()
-    Vc = torch.randn(s.nkv, max_len, 128, generator=g).bfloat16()
+    Kc = torch.randn(s.nkv, max_len, 128, generator=g).to(CDT[cache])
+    Vc = torch.randn(s.nkv, max_len, 128, generator=g).to(CDT[cache])
     rows = torch.randn(T, (s.nq + 2 * s.nkv) * 128, generator=g)
     qn = 1 + 0.02 * torch.randn(128, generator=g)
     kn = 1 + 0.02 * torch.randn(128, generator=g)
     return Kc, Vc, rows, qn, kn
 
 
+@pytest.mark.parametrize("cache", ["bf16", "f32"])
 @pytest.mark.parametrize("pos0,T", [(0, 96), (0, 160), (50, 37), (200, 300), (0, 1), (127, 2)])
-def test_prefill_matches_oracle_and_decode_steps(cuda, pos0, T):
-    """The causal GQA prefill on the tensor cores: outputs within the bf16 bar of the float64 oracle
-    (a run of decode steps), and the appended cache rows bit-identical to those the decode kernel
-    writes token by token."""
+def test_prefill_matches_oracle_and_decode_steps(cuda, pos0, T, cache):
+    """The causal GQA prefill (bf16: tensor cores; fp32: the parity mode): outputs within the bar of
+    the float64 oracle (a run of decode steps), and the appended cache rows bit-identical to those the
+    decode kernel writes token by token."""
     s = W.C3
     max_len = 1536
-    Kc, Vc, rows, qn, kn = _prefill_case(cuda, max_len, pos0, T, seed=pos0 * 7 + T)
-    ta = qwen3.TalkerAttention(1, s.nq, s.nkv, max_len, s.theta, s.eps, cuda, torch.bfloat16)
+    tol = BF16_TOL if cache == "bf16" else FP32_TOL
+    Kc, Vc, rows, qn, kn = _prefill_case(cuda, max_len, pos0, T, seed=pos0 * 7 + T, cache=cache)
+    ta = qwen3.TalkerAttention(1, s.nq, s.nkv, max_len, s.theta, s.eps, cuda, CDT[cache])
     rope = ta.rope
     f = lambda t: t.to(cuda).contiguous()
     K1, V1 = f(Kc), f(Vc)
@@ -300,13 +302,14 @@ def test_prefill_matches_oracle_and_decode_steps(cuda, pos0, T):
         dec.append(o.clone())
     torch.cuda.synchronize()
     lo, hi = pos0, pos0 + T
-    assert torch.equal(K1[:, lo:hi].view(torch.int16), ta.k[0][:, lo:hi].view(torch.int16))
-    assert torch.equal(V1[:, lo:hi].view(torch.int16), ta.v[0][:, lo:hi].view(torch.int16))
-    assert torch.equal(K1[:, :lo].view(torch.int16), f(Kc)[:, :lo].view(torch.int16))  # the prefix untouched
+    iv = torch.int16 if cache == "bf16" else torch.int32
+    assert torch.equal(K1[:, lo:hi].view(iv), ta.k[0][:, lo:hi].view(iv))
+    assert torch.equal(V1[:, lo:hi].view(iv), ta.v[0][:, lo:hi].view(iv))
+    assert torch.equal(K1[:, :lo].view(iv), f(Kc)[:, :lo].view(iv))  # the prefix untouched
     Kh, Vh = host(f(Kc)).astype(np.float64), host(f(Vc)).astype(np.float64)
-    ref = Q.prefill(rows.numpy(), qn.numpy(), kn.numpy(), s.eps, host(rope), Kh, Vh, pos0, s.nq, s.nkv, "bf16")
-    assert rel_l2(host(out), ref) < BF16_TOL
-    assert rel_l2(host(out), host(torch.stack(dec))) < BF16_TOL
+    ref = Q.prefill(rows.numpy(), qn.numpy(), kn.numpy(), s.eps, host(rope), Kh, Vh, pos0, s.nq, s.nkv, cache)
+    assert rel_l2(host(out), ref) < tol
+    assert rel_l2(host(out), host(torch.stack(dec))) < tol
 
 
 def test_prefill_errors(cuda):
@@ -317,7 +320,7 @@ def test_prefill_errors(cuda):
     w = torch.ones(128, device=cuda)
     rope = torch.zeros(max_len, 128, device=cuda)
     with pytest.raises(ValueError):
-        ops.prefill_attention(rows, w, w, 1e-6, rope, K.float(), K.float(), 0, max_len, s.nq, s.nkv)
+        ops.prefill_attention(rows, w, w, 1e-6, rope, K, K.float(), 0, max_len, s.nq, s.nkv)  # mixed dtypes
     from sokutou_b200._lib import SokutouError
     with pytest.raises(SokutouError):
         ops.prefill_attention(rows, w, w, 1e-6, rope, K, K.clone(), 60, max_len, s.nq, s.nkv)  # 60 + 8 > 64
