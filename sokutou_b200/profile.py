@@ -245,3 +245,7 @@ def _cpu_dit(shape, B) -> dict:
         times.append(time.perf_counter() - t0)
     t = sorted(times)[1]
     return {"us_per_call": round(t * 1e6, 1), "TFLOP/s": round(shape.flops(B) / t / 1e12, 4), "cores": os.cpu_count()}
+
+
+if __name__ == "__main__":
+    main()

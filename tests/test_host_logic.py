@@ -60,3 +60,14 @@ def test_serving_requests_seeded():
     assert all(96 <= s <= 384 for k, s in r if k == "dit")
     assert all(200 <= s <= 1500 for k, s in r if k == "decode")
     assert r == W.serving_requests(0)
+
+
+def test_profile_module_runs_as_a_script():
+    """`python -m sokutou_b200.profile` parses its arguments (no GPU needed for --help)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-m", "sokutou_b200.profile", "--help"], cwd=root, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and "--case" in r.stdout
