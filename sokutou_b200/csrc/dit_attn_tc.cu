@@ -46,6 +46,8 @@ constexpr int kLaunchRegs = 168, kSoftmaxRegs = 232, kControlRegs = 40;
 static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreadsTC * kLaunchRegs, "register split over budget");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
+constexpr int kMaxLiveTiles = 64;     // key tiles per CTA up to which fully masked tiles are skipped
+constexpr int kWarpScan0 = 10;        // warps 10-11: the masked-tile scan (SKIP launches)
 
 template <int HD>
 struct TcCfg;
@@ -57,6 +59,15 @@ template <>
 struct TcCfg<128> {  // 32 + 2*32 + 2*32 + 2*32 = 224 KB
   static constexpr int NSK = 2, NSV = 2;
 };
+
+// Key tiles always run, masked or not: every latent tile and at least the first NSK (the producer and
+// the MMA issuer start on these before the masked-tile scan has finished). The rest are the SKIP
+// candidates: in the engine's CFG batches the conditioning tiles, whole text tiles masked in the
+// text-uncond row and whole speaker tiles in the speaker-uncond row (engine/bucket.py:252-258).
+template <int HD>
+__host__ __device__ constexpr int head_tiles(int n_lat, int ntiles) {
+  return n_lat > TcCfg<HD>::NSK ? (n_lat < ntiles ? n_lat : ntiles) : (TcCfg<HD>::NSK < ntiles ? TcCfg<HD>::NSK : ntiles);
+}
 
 template <int HD>
 struct TcLayout {
@@ -74,10 +85,13 @@ struct TcLayout {
   static constexpr int OFF_BIAS = OFF_P + 2 * P_BYTES;
   static constexpr int OFF_BAR = OFF_BIAS + 4 * kBN * 4;
   // q_full, k_full/k_empty[NSK], v_full/v_empty[NSV], s_full[2], s_free[2], p_full[2], o_done[2], mma_done,
-  // and for the fused block: q_free, gate_full
-  static constexpr int NBAR = 1 + 2 * NSK + 2 * NSV + 8 + 1 + 2;
+  // for the fused block: q_free, gate_full; live_ready (SKIP: the list of key tiles to run is built)
+  static constexpr int NBAR = 1 + 2 * NSK + 2 * NSV + 8 + 1 + 2 + 1;
   static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
-  static constexpr int BYTES = OFF_TMEM + 16;
+  // SKIP: [0, 8) bit mask of the key tiles to run, [8, 12) their count, [16, 16 + kMaxLiveTiles) the
+  // tile indices in order
+  static constexpr int OFF_LIVE = OFF_TMEM + 16;
+  static constexpr int BYTES = OFF_LIVE + 16 + kMaxLiveTiles;
   // The dynamic shared-memory base is 1024-byte aligned on sm_100 (checked at run time); the
   // 128B-swizzled tiles need that alignment.
   static constexpr int SMEM_ALLOC = BYTES;
@@ -173,7 +187,13 @@ __device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloa
 // tiles also come straight from o4 (tmV over o4) instead of the producer's (B, H, L, hd) buffer.
 // CAUSAL = true: key j is visible to query row p only if j <= q_pos0 + p (the Qwen3 prefill); key tiles
 // past the CTA's last row are skipped, and the tiles that straddle the diagonal are masked per element.
-template <int HD, bool FUSED, bool VO4, bool CAUSAL>
+// SKIP = true (launched when there is a bias and more than head_tiles key tiles, at most kMaxLiveTiles):
+// a key tile past the head tiles whose every key has a -inf bias adds nothing to any row and is not
+// run. Warps 10-11 scan those tiles' bias at the start and publish the list of tiles to run through
+// live_ready; the producer, the MMA issuer and the softmax warpgroups work on the head tiles meanwhile
+// and read the list only when they get past them. Counts of tiles below are positions in that list;
+// tile_bias and the TMA coordinates take the key tile from it.
+template <int HD, bool FUSED, bool VO4, bool CAUSAL, bool SKIP>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
@@ -202,7 +222,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* mma_done = o_done + 2;
   uint64_t* q_free = mma_done + 1;     // fused: every S = Q·Kᵀ done, the Q area may take the gate tile
   uint64_t* gate_full = q_free + 1;    // fused: gate tile landed
+  uint64_t* live_ready = gate_full + 1;  // SKIP: the list of key tiles to run is in place
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::OFF_TMEM);
+  unsigned long long* live_mask = reinterpret_cast<unsigned long long*>(smem + Ly::OFF_LIVE);
+  int* n_live_s = reinterpret_cast<int*>(smem + Ly::OFF_LIVE + 8);
+  uint8_t* live_map = smem + Ly::OFF_LIVE + 16;
   float* bias_s = reinterpret_cast<float*>(smem + Ly::OFF_BIAS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -211,6 +235,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   // causal: only the latent key tiles up to this CTA's last query row
   const int n_lat = CAUSAL ? min(n_lat_all, (prm.q_pos0 + q0 + kBM - 1) / kBN + 1) : n_lat_all;
   const int ntiles = n_lat + n_ctx;
+  const int kHead = head_tiles<HD>(n_lat, ntiles);  // list entries below kHead are the tiles themselves
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -232,6 +257,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (FUSED) {
       mbar_init(q_free, 1);
       mbar_init(gate_full, 1);
+    }
+    if (SKIP) {
+      mbar_init(live_ready, 1);
+      *live_mask = kHead >= 64 ? ~0ull : (1ull << kHead) - 1;  // the head tiles; the scan adds the others
     }
     fence_mbar_init();
   }
@@ -279,38 +308,47 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       int jk = 0, jv = 0;
       bool ok = true;
+      // SKIP: list entries known to exist — the head tiles until the list is published
+      bool known = !SKIP;
+      int nt = SKIP ? kHead : ntiles;
       const uint64_t t0 = globaltimer_ns();
       uint32_t spins = 0;
-      while (ok && (jk < ntiles || jv < ntiles)) {
+      while (ok && (!known || jk < nt || jv < nt)) {
         bool progress = false;
-        if (jk < ntiles && (jk < NSK || mbar_test(&k_empty[jk % NSK], ((jk / NSK) - 1) & 1))) {
+        if (SKIP && !known && mbar_test(live_ready, 0)) {
+          known = true;
+          nt = *n_live_s;
+        }
+        if (jk < nt && (jk < NSK || mbar_test(&k_empty[jk % NSK], ((jk / NSK) - 1) & 1))) {
           const int s = jk % NSK;
+          const int tk = (SKIP && jk >= kHead) ? live_map[jk] : jk;  // key tile of list entry jk
           uint8_t* dst = smem + Ly::OFF_K + s * Ly::KV_BYTES;
           mbar_arrive_expect_tx(&k_full[s], Ly::KV_BYTES);
-          if (jk < n_lat) {
+          if (tk < n_lat) {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, jk * kBN, lzk);
+              tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, tk * kBN, lzk);
           } else {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_4d(dst + c * (kBN * 128), &tmKc, &k_full[s], c * 64, h, (jk - n_lat) * kBN, bc);
+              tma_load_4d(dst + c * (kBN * 128), &tmKc, &k_full[s], c * 64, h, (tk - n_lat) * kBN, bc);
           }
           ++jk;
           progress = true;
         }
-        if (jv < ntiles && jv < jk && (jv < NSV || mbar_test(&v_empty[jv % NSV], ((jv / NSV) - 1) & 1))) {
+        if (jv < nt && jv < jk && (jv < NSV || mbar_test(&v_empty[jv % NSV], ((jv / NSV) - 1) & 1))) {
           const int s = jv % NSV;
+          const int tv = (SKIP && jv >= kHead) ? live_map[jv] : jv;
           uint8_t* dst = smem + Ly::OFF_V + s * Ly::KV_BYTES;
           mbar_arrive_expect_tx(&v_full[s], Ly::KV_BYTES);
-          if (jv < n_lat) {
+          if (tv < n_lat) {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_3d(dst + c * (kBN * 128), &tmV, &v_full[s], xv + c * 64, jv * kBN, lzv);
+              tma_load_3d(dst + c * (kBN * 128), &tmV, &v_full[s], xv + c * 64, tv * kBN, lzv);
           } else {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_4d(dst + c * (kBN * 128), &tmVc, &v_full[s], c * 64, h, (jv - n_lat) * kBN, bc);
+              tma_load_4d(dst + c * (kBN * 128), &tmVc, &v_full[s], c * 64, h, (tv - n_lat) * kBN, bc);
           }
           ++jv;
           progress = true;
@@ -375,15 +413,23 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tc_commit(&v_empty[sv]);
       };
       int js = 0, jp = 0;
+      // SKIP: list entries known to exist — the head tiles until the list is published
+      bool known = !SKIP;
+      int nt = SKIP ? kHead : ntiles;
       const uint64_t t0 = globaltimer_ns();
       uint32_t spins = 0;
-      while (ok && jp < ntiles) {
+      while (ok && (!known || jp < nt)) {
         bool progress = false;
-        if (js < ntiles && js < jp + 4 && mbar_test(&k_full[js % NSK], (js / NSK) & 1) &&
+        if (SKIP && !known && mbar_test(live_ready, 0)) {
+          known = true;
+          nt = *n_live_s;
+          if (FUSED && js == nt) tc_commit(q_free);  // the head tiles were all there is
+        }
+        if (js < nt && js < jp + 4 && mbar_test(&k_full[js % NSK], (js / NSK) & 1) &&
             (js < 2 || mbar_test(&s_free[js & 1], ((js - 2) >> 1) & 1))) {
           ok = issue_s(js);  // its waits are already satisfied
           ++js;
-          if (FUSED && js == ntiles) tc_commit(q_free);  // Q is read by no further MMA
+          if (FUSED && known && js == nt) tc_commit(q_free);  // Q is read by no further MMA
           progress = true;
         }
         if (ok && jp < js && mbar_test(&p_full[jp & 1], (jp >> 1) & 1) &&
@@ -400,6 +446,44 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       tc_commit(mma_done);
       mbar_wait(mma_done, 0, prm.err);
     }
+  } else if (SKIP && warp >= kWarpScan0) {
+    // ------------------------------------------------------------------ masked-tile scan (warps 10-11)
+    // warp w takes tiles kHead + w, + 2, ... two at a time, lane l testing keys l, l + 32, l + 64, l + 96
+    // of each: 16-bit loads compared with the bits of a bf16 -inf (0xff80), so a tile runs if any key's
+    // bias is anything else (NaN included, as in the softmax). Integer work on few registers, so that
+    // all eight loads of a lane are in flight together.
+    const unsigned short* brow = reinterpret_cast<const unsigned short*>(prm.bias) + (size_t)b * prm.bias_bs;
+    for (int j0 = kHead + (warp - kWarpScan0); j0 < ntiles; j0 += 4) {
+      unsigned short bits[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = j0 + 2 * (e >> 2), col = lane + 32 * (e & 3);
+        // key of column col of tile j: latent keys [0, Lk), then the conditioning keys [Lk, Lk + S)
+        const int kk = j < n_lat ? j * kBN + col : (j - n_lat) * kBN + col;
+        const bool in = j < ntiles && (j < n_lat ? kk < prm.Lk : kk < prm.S);
+        const int key = j < n_lat ? kk : prm.Lk + kk;
+        bits[e] = (in && SK_INB(key < prm.Lk + prm.S, prm.err)) ? __ldg(brow + key) : (unsigned short)0xff80u;
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const bool any = (bits[4 * u] != 0xff80u) | (bits[4 * u + 1] != 0xff80u) | (bits[4 * u + 2] != 0xff80u) |
+                         (bits[4 * u + 3] != 0xff80u);
+        if (__any_sync(0xffffffffu, any) && lane == 0) atomicOr(live_mask, 1ull << (j0 + 2 * u));
+      }
+    }
+    named_bar_sync(4, 64);
+    if (warp == kWarpScan0) {  // the list: tiles with their bit set (the head tiles among them), in order
+      const unsigned long long mk = *reinterpret_cast<volatile unsigned long long*>(live_mask);
+      const unsigned lo = (unsigned)mk, hi = (unsigned)(mk >> 32);
+      const unsigned below = (1u << lane) - 1u;
+      if ((lo >> lane) & 1u) live_map[__popc(lo & below)] = (uint8_t)lane;
+      if ((hi >> lane) & 1u) live_map[__popc(lo) + __popc(hi & below)] = (uint8_t)(lane + 32);
+      __syncwarp();
+      if (lane == 0) {
+        *n_live_s = __popc(lo) + __popc(hi);
+        mbar_arrive(live_ready);
+      }
+    }
   }
   } else {
     // ------------------------------------------------------------------ softmax warpgroups (warps 0-7)
@@ -412,12 +496,27 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const float2 sl2 = make_float2(prm.scale_log2, prm.scale_log2);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    // SKIP: list entries known to exist — the head tiles until the list is read (kHead >= 2, so
+    // entry wg is tile wg)
+    int nt = SKIP ? kHead : ntiles;
+    bool known = !SKIP;
     float bnext = (wg < ntiles) ? tile_bias(prm, bias, b, wg, n_lat, row) : 0.f;
-    for (int j = wg; j < ntiles && ok; j += 2) {
-      const int it = j >> 1;  // this warpgroup's tile count so far
+    for (int i = wg; ok; i += 2) {
+      if (SKIP && !known && i + 2 >= kHead) {  // the next prefetch may need the list
+        known = true;
+        if (!mbar_wait(live_ready, 0, prm.err)) {
+          ok = false;
+          break;
+        }
+        nt = *n_live_s;
+      }
+      if (i >= nt) break;
+      const int j = (SKIP && i >= kHead) ? live_map[i] : i;  // the key tile of list entry i
+      const int it = i >> 1;  // this warpgroup's tile count so far
       float* bt = bias_s + (wg * 2 + (it & 1)) * kBN;
       if (SK_INB(row < kBN && wg * 2 + (it & 1) < 4, prm.err)) bt[row] = bnext;
-      if (j + 2 < ntiles) bnext = tile_bias(prm, bias, b, j + 2, n_lat, row);  // lands during this tile
+      if (i + 2 < nt)  // lands during this tile
+        bnext = tile_bias(prm, bias, b, (SKIP && i + 2 >= kHead) ? live_map[i + 2] : i + 2, n_lat, row);
       named_bar_sync(1 + wg, 128);
       if (!mbar_wait(&s_full[wg], it & 1, prm.err)) {
         ok = false;
@@ -462,15 +561,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const float mt = fmaxf(fmaxf(mt0, mt1), fmaxf(mt2, mt3));
       const float m_new = fmaxf(m_run, mt);
       const bool want = m_new > m_run + kRescaleLog2;  // false while every key seen is masked
-      // P tile and O rows of this warpgroup were last used by PV_{j-2}
-      if (j >= 2 && !mbar_wait(&o_done[wg], ((j - 2) >> 1) & 1, prm.err)) {
+      // P tile and O rows of this warpgroup were last used by the P·V of list entry i - 2
+      if (i >= 2 && !mbar_wait(&o_done[wg], ((i - 2) >> 1) & 1, prm.err)) {
         ok = false;
         break;
       }
       if (__any_sync(0xffffffffu, want)) {
         // warp-uniform: every lane of the warp moves to its exact current max
         const float alpha = (m_new == -INFINITY) ? 1.f : ex2_approx(m_run - m_new);
-        if (j >= 2) {
+        if (i >= 2) {
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
@@ -478,7 +577,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             tmem_ld32(tO + wg * HD + lane_off + c * 32, ov);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            for (int e = 0; e < 32; ++e) ov[e] *= alpha;
             tmem_st32(tO + wg * HD + lane_off + c * 32, ov);
           }
           tmem_wait_st();
@@ -537,8 +636,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     named_bar_sync(3, 256);
     bool okk = ok;
     for (int w = 0; w < 2 && okk; ++w) {  // both accumulators complete (the last PV of each)
-      const int jl = ((ntiles - 1 - w) >> 1) * 2 + w;
-      if (jl < ntiles && jl >= 0) okk = mbar_wait(&o_done[w], (jl >> 1) & 1, prm.err);
+      const int jl = ((nt - 1 - w) >> 1) * 2 + w;
+      if (jl < nt && jl >= 0) okk = mbar_wait(&o_done[w], (jl >> 1) & 1, prm.err);
     }
     if (FUSED && okk) okk = mbar_wait(gate_full, 0, prm.err);
     okk = __all_sync(0xffffffffu, okk);
@@ -704,14 +803,30 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     if (!make_map(&my, prm.y, 4, dims, str, box)) return SK_ERR_CUDA;
   }
   const int smem = Ly::SMEM_ALLOC;
-  static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(attn_tc_kernel<HD, FUSED, VO4, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
+  static int sm_count[64] = {};
+  if (dev >= 0 && dev < 64 && sm_count[dev] == 0 &&
+      cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return SK_ERR_CUDA;
+  // Masked-tile skipping (never in the causal form): with a bias, more key tiles than the head tiles,
+  // and more CTAs than SMs. One CTA fills an SM (all of TMEM), so in a single wave the call lasts as
+  // long as its longest CTA, and in the engine's CFG batches the cond row has no whole tile masked:
+  // skipping pays only where CTAs queue for SMs and the shortened ones let the queue drain sooner,
+  // while the list of tiles costs each CTA about 0.7 us.
+  const int n_lat = (Lk + kBN - 1) / kBN, ntiles = n_lat + (S + kBN - 1) / kBN;
+  const long long ctas = (long long)((L + kBM - 1) / kBM) * H * B;
+  const bool skip = !CAUSAL && prm.bias != nullptr && ntiles > head_tiles<HD>(n_lat, ntiles) &&
+                    ntiles <= kMaxLiveTiles && dev >= 0 && dev < 64 && ctas > sm_count[dev];
+  auto kern = attn_tc_kernel<HD, FUSED, VO4, CAUSAL, false>;
+  if constexpr (!CAUSAL) {
+    if (skip) kern = attn_tc_kernel<HD, FUSED, VO4, CAUSAL, true>;
+  }
+  static bool attr_done[2][64] = {};
+  if (dev >= 0 && dev < 64 && !attr_done[skip][dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return SK_ERR_CUDA;
-    attr_done[dev] = true;
+    attr_done[skip][dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((L + kBM - 1) / kBM, H, B);
@@ -723,8 +838,7 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = sk::kUsePdl ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<HD, FUSED, VO4, CAUSAL>, mq, mk, mv, mkc, mvc, my, mg, prm) !=
-      cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mkc, mvc, my, mg, prm) != cudaSuccess)
     return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }

@@ -152,6 +152,45 @@ def test_fully_masked_row_and_no_bias(cuda, name):
     assert rel_l2(host(y0), ref0) < tol(dt)
 
 
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("Lk,S", [(700, 520), (256, 1100), (8300, 200)])
+def test_fully_masked_key_tiles(cuda, hd, Lk, S):
+    """Key tiles past the latent ones whose every key is masked are not run by the bf16 kernel when the
+    grid has more CTAs than SMs (here 6 rows x 16 heads x 2 query tiles = 192) and at most 64 key tiles
+    (8300 latent keys = 65 tiles take the path without skipping): rows with dead conditioning tiles, a
+    row with one live key in its last tile, a fully masked row, a row masked past its first two tiles,
+    and random single-key masks that leave no tile dead. Heads are independent, so two of the 16 are
+    checked against the oracle."""
+    torch.manual_seed(Lk + S + hd)
+    B, H, L = 6, 16, 256 if Lk < 8000 else 128
+    dt = torch.bfloat16
+    q = torch.randn(B, H, L, hd, device=cuda).to(dt)
+    kl, vl = (torch.randn(B, H, Lk, hd, device=cuda).to(dt) for _ in range(2))
+    kc, vc = (torch.randn(S, H, hd, device=cuda).to(dt) for _ in range(2))
+    K = Lk + S
+    bias = torch.zeros(B, K, device=cuda)
+    bias[1, Lk:Lk + min(S, 128)] = float("-inf")          # row 1: the first conditioning tile ...
+    for t in (2, 4):                                      # ... and more whole conditioning tiles
+        bias[1, Lk + t * 128:Lk + min(S, (t + 1) * 128)] = float("-inf")
+    bias[1, 300:310] = float("-inf")
+    bias[2] = float("-inf")                               # row 2: one live key, in the last tile
+    bias[2, K - 1] = 0.0
+    bias[3] = float("-inf")                               # row 3: nothing visible -> zeros
+    bias[4, 256:] = float("-inf")                         # row 4: only the first two latent tiles
+    bias[5, torch.rand(K, device=cuda) < 0.5] = float("-inf")  # row 5: no tile entirely masked
+    bias = bias.to(dt)
+    y = ops.dit_attention(q, kl, vl, kc, vc, bias)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.all(y[3] == 0)
+    hs = [0, H - 1]
+    ref = D.dit_attention(host(q[:, hs]), host(kl[:, hs]), host(vl[:, hs]), host(kc[:, hs])[None],
+                          host(vc[:, hs])[None], host(bias))
+    got = host(y[:, :, hs])
+    for r in (0, 1, 2, 4, 5):
+        assert rel_l2(got[r], ref[r]) < BF16_TOL, r
+
+
 @pytest.mark.parametrize("name", ["bf16", "f32"])
 def test_per_batch_ctx_and_shared_bias(cuda, name):
     dt = DT[name]

@@ -68,7 +68,8 @@ def test_layer_bit_identical_to_separate_calls(cuda, B, L, H, hd, S):
 
 
 @pytest.mark.parametrize("B,L,H,hd,S", [(3, 128, 4, 64, 256), (3, 97, 4, 64, 7), (3, 129, 2, 128, 200),
-                                         (1, 512, 2, 128, 512), (2, 1, 2, 64, 5)])
+                                         (1, 512, 2, 128, 512), (3, 512, 16, 128, 512), (3, 768, 12, 64, 256),
+                                         (2, 1, 2, 64, 5)])
 def test_layer_matches_oracle(cuda, B, L, H, hd, S):
     o4, qk_w, freqs, kc, vc, bias = _inputs(cuda, B, L, H, hd, S, seed=7 + L)
     out = ops.dit_attention_layer(o4, qk_w, freqs, B, L, H, hd, 1e-6, kc, vc, bias).float().cpu().numpy()
