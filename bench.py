@@ -484,6 +484,52 @@ def layer_block(device, dist: Dist, calls: int = 120, sets: int = 4) -> dict:
     return out
 
 
+# ------------------------------------------------------------------------------------------- DiT GEMMs
+GEMM_SHAPES = (  # name, M (= B·L rows), N, K: the attention block's projections at B = 3, L = 512
+    ("c1_w_qkvg_b3", 1536, 4 * 768, 768), ("c1_w_o_b3", 1536, 768, 768),
+    ("c2_w_qkvg_b3", 1536, 4 * 2048, 2048), ("c2_w_o_b3", 1536, 2048, 2048),
+)
+
+
+def dit_gemm(device, dist: Dist, calls: int = 60, sets: int = 4) -> dict:
+    """The DiT projections y = x·wᵀ (engine/fused.py:262-264) on the tcgen05 GEMM (sk_dit_linear) and,
+    beside it, torch's F.linear (cuBLAS) on the same inputs; `sets` distinct (x, w) pairs rotated over
+    `calls` graph-replayed calls. Reports microseconds per call and TFLOP/s (2·M·N·K per call)."""
+    import torch.nn.functional as F
+    from sokutou_b200 import ops
+    out = {}
+    for name, M, N, K in GEMM_SHAPES:
+        g = torch.Generator(device=device).manual_seed(9)
+        ins = [((torch.randn(M, K, device=device, generator=g)).bfloat16(),
+                (torch.randn(N, K, device=device, generator=g) * K ** -0.5).bfloat16(),
+                torch.empty(M, N, device=device, dtype=torch.bfloat16)) for _ in range(sets)]
+        res = {"M": M, "N": N, "K": K}
+        for impl in ("sk", "cublas"):
+            if impl == "sk":
+                run = lambda: [ops.dit_linear(ins[i % sets][0], ins[i % sets][1], out=ins[i % sets][2])
+                               for i in range(calls)]
+            else:
+                run = lambda: [torch.matmul(ins[i % sets][0], ins[i % sets][1].t(), out=ins[i % sets][2])
+                               for i in range(calls)]
+            st = torch.cuda.Stream(device)
+            st.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(st):
+                run()
+            torch.cuda.current_stream(device).wait_stream(st)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                run()
+            ms = time_graphs([gr], 3, 3, dist)
+            us = ms * 1e3 / (3 * calls)
+            key = "us" if impl == "sk" else "cublas_us"
+            res[key] = round(us, 3)
+            res["tflops" if impl == "sk" else "cublas_tflops"] = round(2 * M * N * K / (us * 1e-6) / 1e12, 1)
+            del gr
+        out[name] = res
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------------------------------- prefill
 def prefill_bench(device, dist: Dist) -> dict:
     """The c3 prompt (and a 160-token one) through all 28 talker layers' prefill attention, graph-replayed,
@@ -643,6 +689,7 @@ def main():
 
     # ---- fused attention block vs its three launches; Qwen3 prompt prefill
     blocks = layer_block(dev, dist)
+    gemm = dit_gemm(dev, dist)
     prefill = prefill_bench(dev, dist)
 
     # ---- c4 serving
@@ -675,7 +722,7 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": UNIT,
                          "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} bf16 burst",
                          "frac_of_spec": round(achieved / SPEC["bf16_tflops"], 4), "traffic": traffic},
-            "c2": c2_res, "c3": c3_res, "layer_block": blocks, "prefill": prefill, "serving": serv, "cpu_baseline": cpu,
+            "c2": c2_res, "c3": c3_res, "layer_block": blocks, "dit_gemm": gemm, "prefill": prefill, "serving": serv, "cpu_baseline": cpu,
             "clocks": clk.summary(), "device_error": err,
         }
         print(json.dumps(line), flush=True)

@@ -159,6 +159,19 @@ SK_API int sk_dit_attention_layer(const void* o4, const float* qk_w, const float
 SK_API int sk_dit_gate(const void* y, const void* o4, void* out, long long rows, int D, int dtype,
                        int out_dtype, float out_scale, void* stream);
 
+/*
+ * One DiT projection: y = x · wᵀ (F.linear without bias), the `mm` of engine/fused.py:262-264 that
+ * the engine calls for w_qkvg, w_o, w_13 and w_2 (engine/fused.py:293-310). tcgen05 tiles of
+ * 128 x 256 with fp32 accumulation, rounded once to bf16.
+ *
+ *   x      : (M, K) bf16 rows (the step's latent rows)
+ *   w      : (N, K) bf16, the weight as nn.Linear stores it
+ *   y      : (M, N) bf16; must not overlap x or w
+ *   dtype  : SK_BF16 only (the fp32 parity mode keeps the library GEMM)
+ *   K and N multiples of 8; all pointers 16-byte aligned.
+ */
+SK_API int sk_dit_linear(const void* x, const void* w, void* y, int M, int N, int K, int dtype, void* stream);
+
 /* ---- 2. Qwen3 talker decode attention --------------------------------------------------------- */
 
 /* Bytes of scratch sk_decode_attention needs for a cache of max_len positions. */

@@ -10,6 +10,8 @@ Restates, in numpy float64:
     [latent | text | speaker] (engine/fast.py:167-168);
   - the consumer `gate` (engine/fused.py:182-190): y · sigmoid(gate) in float32, rounded once, with
     the FP8 e4m3 output form (engine/fused.py:52-76).
+  - the projections around them, `mm` = F.linear(x, w) (engine/fused.py:262-264): x · wᵀ in float64,
+    rounded once to the output type.
 
 The RoPE frequency table of Irodori-TTS (`model._rope_freqs`, engine/fast.py:264) lives in the
 third-party package irodori_tts @ 7ed4374 (not present here); `rope_freqs` restates the
@@ -184,6 +186,14 @@ def e4m3_decode(c) -> np.ndarray:
     mag = _e4m3_table()[np.minimum(c & 0x7F, 0x7E)]
     mag = np.where((c & 0x7F) == 0x7F, np.nan, mag)
     return np.where(c & 0x80, -mag, mag).astype(np.float32)
+
+
+def linear(x, w, out: str = "f32") -> np.ndarray:
+    """F.linear(x, w) without bias (engine/fused.py:262-264): x (M, K) · w (N, K)ᵀ in float64, rounded
+    once to `out` ("f32" or "bf16", round to nearest even)."""
+    y = np.asarray(x, np.float64) @ np.asarray(w, np.float64).T
+    y = y.astype(np.float32)
+    return bf16_round(y) if out == "bf16" else y
 
 
 def gate(y, o4, out: str = "f32", out_scale: float = 1.0) -> np.ndarray:

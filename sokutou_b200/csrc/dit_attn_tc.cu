@@ -717,34 +717,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 }
 
 // ---- host ------------------------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-// bf16 tensor map, 128-byte swizzle, box = {64, box_rows...}; dims/strides innermost first.
-static bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_b,
-                     const cuuint32_t* box) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  cuuint32_t es[5] = {1, 1, 1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides_b, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // q (B, H, L, hd), k_lat (B, H, Lk, hd); v_lat (B, H, Lk, hd), or with VO4 the projection rows o4;
 // o4 (B·L, 4·D): the gate source of the fused block (unused otherwise).
 // kv_rows: rows per head in the key/value buffers (Lk for the DiT; the cache's max_len for the prefill).
@@ -759,7 +731,7 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)L, (cuuint64_t)B * H};
     cuuint64_t str[2] = {(cuuint64_t)HD * 2, (cuuint64_t)L * HD * 2};
     cuuint32_t box[3] = {64, kBM, 1};
-    if (!make_map(&mq, q, 3, dims, str, box)) return SK_ERR_CUDA;
+    if (!sk_make_map_bf16(&mq, q, 3, dims, str, box)) return SK_ERR_CUDA;
   }
   if (Lk > 0) {
     // key/value heads: H / kv_group of them per batch row, kv_rows rows apart
@@ -767,8 +739,8 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)Lk, (cuuint64_t)B * (H / prm.kv_group)};
     cuuint64_t str[2] = {(cuuint64_t)HD * 2, (cuuint64_t)rows * HD * 2};
     cuuint32_t box[3] = {64, kBN, 1};
-    if (!make_map(&mk, k_lat, 3, dims, str, box)) return SK_ERR_CUDA;
-    if (!VO4 && !make_map(&mv, v_lat, 3, dims, str, box)) return SK_ERR_CUDA;
+    if (!sk_make_map_bf16(&mk, k_lat, 3, dims, str, box)) return SK_ERR_CUDA;
+    if (!VO4 && !sk_make_map_bf16(&mv, v_lat, 3, dims, str, box)) return SK_ERR_CUDA;
   } else {
     mk = mq;  // never read: no latent key tiles
     mv = mq;
@@ -779,7 +751,7 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     cuuint64_t str[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2,
                          (cuuint64_t)(prm.ctx_batched ? ctx_bs * 2 : (long long)S * H * HD * 2)};
     cuuint32_t box[4] = {64, 1, kBN, 1};
-    if (!make_map(&mkc, k_ctx, 4, dims, str, box) || !make_map(&mvc, v_ctx, 4, dims, str, box)) return SK_ERR_CUDA;
+    if (!sk_make_map_bf16(&mkc, k_ctx, 4, dims, str, box) || !sk_make_map_bf16(&mvc, v_ctx, 4, dims, str, box)) return SK_ERR_CUDA;
   } else {
     mkc = mq;  // never read: no conditioning key tiles
     mvc = mq;
@@ -791,7 +763,7 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     cuuint64_t d4[3] = {(cuuint64_t)4 * prm.D, (cuuint64_t)L, (cuuint64_t)B};
     cuuint64_t s4[2] = {(cuuint64_t)4 * prm.D * 2, (cuuint64_t)L * 4 * prm.D * 2};
     cuuint32_t box[3] = {64, kBM, 1};
-    if (!make_map(&mg, o4, 3, d4, s4, box)) return SK_ERR_CUDA;
+    if (!sk_make_map_bf16(&mg, o4, 3, d4, s4, box)) return SK_ERR_CUDA;
     if (VO4) mv = mg;
   }
   CUtensorMap my;
@@ -800,7 +772,7 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
     cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)L, (cuuint64_t)B};
     cuuint64_t str[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2, (cuuint64_t)L * H * HD * 2};
     cuuint32_t box[4] = {64, 1, kBM, 1};
-    if (!make_map(&my, prm.y, 4, dims, str, box)) return SK_ERR_CUDA;
+    if (!sk_make_map_bf16(&my, prm.y, 4, dims, str, box)) return SK_ERR_CUDA;
   }
   const int smem = Ly::SMEM_ALLOC;
   int dev = 0;

@@ -1,0 +1,219 @@
+// DiT projection GEMM, bf16 mode, on the sm_100a tensor cores (tcgen05 + TMEM + TMA):
+//   y (M, N) = x (M, K) · w (N, K)ᵀ
+// F.linear without bias — the `mm` of engine/fused.py:262-264, called for w_qkvg, w_o, w_13 and w_2
+// at engine/fused.py:293-310 (x = the rows of one step's latent batch, w = the layer's weight as
+// nn.Linear stores it). Both operands are K-major, the layout the tensor core reads directly.
+//
+// One CTA computes a 128 x 256 tile of y, 128 threads:
+//   warp 0 (one lane)  TMA producer: per 64-wide k step one x box [128 rows][64] and one w box
+//                      [256 rows][64] (128-byte swizzled) into a ring of kStages slots.
+//   warp 1 (one lane)  MMA issuer: four tcgen05.mma (M 128, N 256, K 16) per k step into one fp32
+//                      TMEM accumulator of 256 columns; each slot is released by tcgen05.commit.
+//   warps 0-3          epilogue: thread r reads TMEM lane r (its row), rounds once to bf16, stages the
+//                      tile 128B-swizzled over the (then idle) ring, and one thread writes it with TMA
+//                      tensor stores; rows and columns past M and N are clipped by the tensor map, and
+//                      k past K reads zeros.
+// Every wait gives up after 2 s (error word, then the CTA unwinds). No TMA multicast.
+#include "sk_common.cuh"
+
+namespace sk {
+namespace lin {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;  // CTA tile; one k step = one 128-byte swizzle row
+constexpr int kStages = 4;
+constexpr int kThreads = 128;
+constexpr int A_BYTES = kBM * kBK * 2;                 // 16 KB
+constexpr int B_BYTES = kBN * kBK * 2;                 // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;         // 48 KB
+constexpr int OFF_BAR = kStages * STAGE_BYTES;         // full[kStages], empty[kStages], mma_done
+constexpr int NBAR = 2 * kStages + 1;
+constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+constexpr int SMEM = OFF_TMEM + 16;
+static_assert(kBN / 64 * kBM * 128 <= OFF_BAR, "the output staging must fit over the ring");
+static_assert(SMEM <= 232448, "shared memory over the 227 KB per-CTA limit");
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                  const __grid_constant__ CUtensorMap tmY, int N, int K, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  if (sbase & 1023u) {  // uniform for the CTA, before any barrier: report and leave
+    if (threadIdx.x == 0) set_dev_error(err, SK_DEVERR_TIMEOUT);
+    return;
+  }
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* empty = full + kStages;
+  uint64_t* mma_done = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  const int nk = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmY);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kBN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // x may come from the kernel launched before this one
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    int issued = 0;
+    for (int kc = 0; kc < nk; ++kc) {
+      const int s = kc % kStages;
+      if (kc >= kStages && !mbar_wait(&empty[s], ((kc / kStages) - 1) & 1, err)) break;
+      uint8_t* a = smem + s * STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+      tma_load_3d(a, &tmX, &full[s], kc * kBK, m0, 0);
+      tma_load_3d(a + A_BYTES, &tmW, &full[s], kc * kBK, n0, 0);
+      issued = kc + 1;
+    }
+    // keep shared memory alive until every copy issued has landed (already true on the normal path)
+    for (int kc = (issued > kStages ? issued - kStages : 0); kc < issued; ++kc)
+      mbar_wait(&full[kc % kStages], (kc / kStages) & 1, err);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN, 0, 0);
+    for (int kc = 0; kc < nk; ++kc) {
+      const int s = kc % kStages;
+      if (!mbar_wait(&full[s], (kc / kStages) & 1, err)) break;
+      tc_fence_after();
+      const uint32_t a = sbase + s * STAGE_BYTES, bw = a + A_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk)
+        tc_mma_ss(tmem, smem_desc_sw128(a + kk * 32, 16, 1024), smem_desc_sw128(bw + kk * 32, 16, 1024), idesc,
+                  (kc > 0 || kk > 0) ? 1u : 0u);
+      tc_commit(&empty[s]);  // the slot is free once these MMAs have read it
+    }
+    tc_commit(mma_done);  // every MMA issued has completed
+  }
+  __syncwarp();
+
+  // ------------------------------------------------------------------ epilogue (warps 0-3)
+  bool ok = mbar_wait(mma_done, 0, err);
+  ok = __all_sync(0xffffffffu, ok);
+  const int row = threadIdx.x;  // TMEM lane == row of the tile
+  if (ok) {
+    tc_fence_after();
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+#pragma unroll 1
+    for (int c = 0; c < kBN / 32; ++c) {
+      float v[32];
+      tmem_ld32(tmem + lane_off + c * 32, v);
+      tmem_wait_ld();
+      // 32 columns = four 16-byte units of the 64-column chunk c / 2
+      uint8_t* chunk = smem + (c >> 1) * (kBM * 128) + row * 128;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]);
+          pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+        }
+        const int unit = (c & 1) * 4 + u;
+        if (SK_INB((c >> 1) * (kBM * 128) + row * 128 + ((unit ^ (row & 7)) << 4) + 16 <= OFF_BAR, err))
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + ((unit ^ (row & 7)) << 4))),
+                       "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3])
+                       : "memory");
+      }
+    }
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+  if (ok && threadIdx.x == 0) {
+#pragma unroll
+    for (int c = 0; c < kBN / 64; ++c)  // column chunks that start inside y (the map clips the rest)
+      if (n0 + c * 64 < N) tma_store_3d(&tmY, smem + c * (kBM * 128), n0 + c * 64, m0, 0);
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kBN);
+  }
+}
+
+}  // namespace lin
+}  // namespace sk
+
+extern "C" int sk_dit_linear(const void* x, const void* w, void* y, int M, int N, int K, int dtype, void* stream) {
+  using namespace sk::lin;
+  if (!x || !w || !y) return SK_ERR_INVALID_ARG;
+  if (M <= 0 || N <= 0 || K <= 0) return SK_ERR_INVALID_ARG;
+  if (dtype != SK_BF16) return SK_ERR_UNSUPPORTED;  // the fp32 mode keeps the library GEMM
+  // tensor maps: 16-byte aligned bases and row strides
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15)
+    return SK_ERR_INVALID_ARG;
+  if (K % 8 || N % 8) return SK_ERR_INVALID_ARG;
+  const int rc = sk_check_device();
+  if (rc != SK_OK) return rc;
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
+  CUtensorMap mx, mw, my;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)M, 1};
+    cuuint64_t str[2] = {(cuuint64_t)K * 2, (cuuint64_t)M * K * 2};
+    cuuint32_t box[3] = {kBK, kBM, 1};
+    if (!sk_make_map_bf16(&mx, x, 3, dims, str, box)) return SK_ERR_CUDA;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)N, 1};
+    cuuint64_t str[2] = {(cuuint64_t)K * 2, (cuuint64_t)N * K * 2};
+    cuuint32_t box[3] = {kBK, kBN, 1};
+    if (!sk_make_map_bf16(&mw, w, 3, dims, str, box)) return SK_ERR_CUDA;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, 1};
+    cuuint64_t str[2] = {(cuuint64_t)N * 2, (cuuint64_t)M * N * 2};
+    cuuint32_t box[3] = {64, kBM, 1};
+    if (!sk_make_map_bf16(&my, y, 3, dims, str, box)) return SK_ERR_CUDA;
+  }
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+      return SK_ERR_CUDA;
+    attr_done[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = sk::kUsePdl ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, linear_kernel, mx, mw, my, N, K, err) != cudaSuccess) return SK_ERR_CUDA;
+  return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
+}

@@ -299,3 +299,7 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) { return __ui
 int* sk_error_word_ptr();
 // Host side (api.cu): SK_OK when the current device is an sm_100 part, else SK_ERR_DEVICE.
 int sk_check_device();
+// Host side (api.cu): bf16 tensor map with 128-byte swizzle, box = {64, ...}; dims and byte strides
+// innermost first; loads past the edges read zeros, stores past them are dropped.
+bool sk_make_map_bf16(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_b,
+                      const cuuint32_t* box);

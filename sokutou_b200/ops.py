@@ -244,6 +244,25 @@ def dit_gate(y: torch.Tensor, o4: torch.Tensor, out: torch.Tensor | None = None,
     return out
 
 
+def dit_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x · wᵀ (F.linear without bias, engine/fused.py:262-264) on the tcgen05 GEMM, bf16 in and out,
+    fp32 accumulation. x (M, K), w (N, K); returns (M, N)."""
+    _cuda_contig("x", x)
+    _cuda_contig("w", w)
+    _need(x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16, "dit_linear runs bf16 (fp32: use F.linear)")
+    _need(x.dim() == 2 and w.dim() == 2 and x.shape[1] == w.shape[1], "x must be (M, K) and w (N, K)")
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), device=x.device, dtype=x.dtype)
+    _cuda_contig("out", out)
+    _need(out.dtype == x.dtype and out.shape == (M, N), f"out must be ({M}, {N}) bf16")
+    with _nvtx("sk_dit_linear"):
+        check(lib().sk_dit_linear(_ptr(x), _ptr(w), _ptr(out), M, N, K, _dtype_code(x.dtype), _stream()),
+              "sk_dit_linear")
+    return out
+
+
 def decode_workspace_bytes(max_len: int, nq: int, nkv: int, hd: int = 128, cache_dtype: torch.dtype = torch.bfloat16) -> int:
     return int(lib().sk_decode_workspace_bytes(max_len, nq, nkv, hd, _dtype_code(cache_dtype)))
 

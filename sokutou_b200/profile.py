@@ -37,6 +37,10 @@ CASES = {
     "decode_T128": ("decode", 128, None), "decode_T512": ("decode", 512, None),
     "decode_T1120": ("decode", 1120, None), "decode_T1500": ("decode", 1500, None),
     "decode_T1120_kvstable": ("decode", 1120, "kv_stable"), "decode_T128_kvstable": ("decode", 128, "kv_stable"),
+    # the projections around the block (M = B·L rows, N, K), tcgen05 GEMM and torch's cuBLAS F.linear
+    "linear_c1_qkvg_b3": ("linear", (1536, 3072, 768), "sk"), "cublas_c1_qkvg_b3": ("linear", (1536, 3072, 768), "cublas"),
+    "linear_c2_qkvg_b3": ("linear", (1536, 8192, 2048), "sk"), "cublas_c2_qkvg_b3": ("linear", (1536, 8192, 2048), "cublas"),
+    "linear_c2_o_b3": ("linear", (1536, 2048, 2048), "sk"), "cublas_c2_o_b3": ("linear", (1536, 2048, 2048), "cublas"),
     # calibration: what a chain of dependent kernels costs on this GPU without any attention work
     "calib_tiny": ("calib", 0, None), "calib_copy_4.6MB": ("calib", 4616192, None),
 }
@@ -127,6 +131,22 @@ def decode_case(T, sets, dev, kv_stable=False):
     return fns, s.layer_bytes(T), "byte"
 
 
+def linear_case(mnk, impl, sets, dev):
+    """y = x·wᵀ (engine/fused.py:262-264) on sk_dit_linear or on torch's F.linear (cuBLAS); work = 2·M·N·K."""
+    M, N, K = mnk
+    g = torch.Generator(device=dev).manual_seed(0)
+    fns = []
+    for _ in range(sets):
+        x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+        w = (torch.randn(N, K, device=dev, generator=g) * K ** -0.5).bfloat16()
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        if impl == "sk":
+            fns.append(lambda x=x, w=w, y=y: ops.dit_linear(x, w, out=y))
+        else:
+            fns.append(lambda x=x, w=w, y=y: torch.matmul(x, w.t(), out=y))
+    return fns, 2 * M * N * K, "flop"
+
+
 def calib_case(nbytes, sets, dev):
     """A dependent chain of torch kernels: a one-element add (launch floor), or a device copy of
     `nbytes` (twice that moved) over 16 rotating buffer pairs so the copies miss L2."""
@@ -158,6 +178,8 @@ def main():
         fns, work, unit = layer_case(x, B, a.sets, dev, fused=(kind == "layer"))
     elif kind == "prefill":
         fns, work, unit = prefill_case(x, a.sets, dev)
+    elif kind == "linear":
+        fns, work, unit = linear_case(x, B, a.sets, dev)
     elif kind == "decode":
         fns, work, unit = decode_case(x, a.sets, dev, kv_stable=(B == "kv_stable"))
     else:
@@ -207,6 +229,8 @@ def main():
 def _shape(kind, x, B):
     if kind in ("dit", "layer", "layer_sep", "prologue", "gate"):
         return {"B": B, "H": x.H, "hd": x.hd, "L": x.L, "text_keys": x.Tb, "speaker_keys": x.Sp}
+    if kind == "linear":
+        return {"M": x[0], "N": x[1], "K": x[2], "impl": B}
     if kind in ("decode", "prefill"):
         s = W.C3
         return {"T": x, "nq": s.nq, "nkv": s.nkv, "hd": s.hd}

@@ -1,0 +1,78 @@
+"""The DiT projection GEMM (sk_dit_linear: y = x·wᵀ, F.linear at engine/fused.py:262-264) on the B200.
+
+Bars: relative L2 <= 1e-2 (the bf16 per-layer bar) against the float64 oracle on the same bf16
+inputs, and <= 3e-3 as the check of this kernel (one bf16 rounding of an fp32 accumulation is about
+1e-3); the same against torch's own cuBLAS F.linear; nothing written outside y.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_l2
+from oracle import dit_attn_ref as D
+from sokutou_b200 import ops
+from sokutou_b200._lib import SokutouError
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [  # M, N, K
+    (1536, 3072, 768), (384, 3072, 768), (1536, 768, 768), (512, 8192, 2048), (1536, 2048, 2048),
+    (128, 256, 64), (97, 200, 72), (1, 8, 8), (130, 264, 136), (300, 520, 1000), (257, 1032, 4104),
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_linear_matches_oracle(cuda, M, N, K):
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, generator=g).bfloat16()
+    w = (torch.randn(N, K, generator=g) * K ** -0.5).bfloat16()
+    buf = torch.full((M * N + 4096,), 3.0, dtype=torch.bfloat16, device=cuda)
+    y = ops.dit_linear(x.to(cuda), w.to(cuda), out=buf[:M * N].view(M, N))
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.all(buf[M * N:] == 3.0)
+    want = D.linear(x.float().numpy(), w.float().numpy(), "f32")
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    err = rel_l2(got, want)
+    assert err < 1e-2 and err < 3e-3, err
+    lib = torch.nn.functional.linear(x.to(cuda), w.to(cuda)).float().cpu().numpy()
+    assert rel_l2(got, lib) < 3e-3
+
+
+def test_linear_graph_replay_and_stream(cuda):
+    M, N, K = 640, 1024, 512
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(M, K, generator=g).bfloat16().to(cuda)
+    w = (torch.randn(N, K, generator=g) * K ** -0.5).bfloat16().to(cuda)
+    y = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        ops.dit_linear(x, w, out=y)
+    torch.cuda.current_stream().wait_stream(st)
+    ref = y.clone()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        ops.dit_linear(x, w, out=y)
+    y.zero_()
+    gr.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+
+
+def test_linear_errors(cuda):
+    x = torch.zeros(4, 12, device=cuda, dtype=torch.bfloat16)
+    w = torch.zeros(16, 12, device=cuda, dtype=torch.bfloat16)
+    with pytest.raises(SokutouError):
+        ops.dit_linear(x, w)  # K = 12 is not a multiple of 8
+    with pytest.raises(ValueError):
+        ops.dit_linear(x.float(), w.float())  # fp32: the library GEMM
+    from sokutou_b200 import _lib
+    x = torch.zeros(4, 16, device=cuda, dtype=torch.bfloat16)
+    y = torch.zeros(4, 16, device=cuda, dtype=torch.bfloat16)
+    call = lambda M, N, K, dtype: _lib.lib().sk_dit_linear(x.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K, dtype, 0)
+    assert call(4, 4, 16, 1) == -2   # float32 unsupported
+    assert call(0, 8, 16, 0) == -1   # empty
+    assert call(4, 12, 16, 0) == -1  # N not a multiple of 8
