@@ -171,6 +171,10 @@ SK_API int sk_dit_gate(const void* y, const void* o4, void* out, long long rows,
  *   K and N multiples of 8; all pointers 16-byte aligned.
  */
 SK_API int sk_dit_linear(const void* x, const void* w, void* y, int M, int N, int K, int dtype, void* stream);
+/* sk_dit_linear with the N width of the CTA tile given: 64, 128 or 256 (0: chosen per call from the
+ * grid it gives, as sk_dit_linear does). */
+SK_API int sk_dit_linear_ex(const void* x, const void* w, void* y, int M, int N, int K, int dtype, int tile_n,
+                            void* stream);
 
 /* ---- 2. Qwen3 talker decode attention --------------------------------------------------------- */
 

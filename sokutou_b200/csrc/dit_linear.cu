@@ -4,11 +4,11 @@
 // at engine/fused.py:293-310 (x = the rows of one step's latent batch, w = the layer's weight as
 // nn.Linear stores it). Both operands are K-major, the layout the tensor core reads directly.
 //
-// One CTA computes a 128 x 256 tile of y, 128 threads:
+// One CTA computes a 128 x BN tile of y (BN = 256, 128 or 64, chosen per call), 128 threads:
 //   warp 0 (one lane)  TMA producer: per 64-wide k step one x box [128 rows][64] and one w box
-//                      [256 rows][64] (128-byte swizzled) into a ring of kStages slots.
-//   warp 1 (one lane)  MMA issuer: four tcgen05.mma (M 128, N 256, K 16) per k step into one fp32
-//                      TMEM accumulator of 256 columns; each slot is released by tcgen05.commit.
+//                      [BN rows][64] (128-byte swizzled) into a ring of kStages slots.
+//   warp 1 (one lane)  MMA issuer: four tcgen05.mma (M 128, N BN, K 16) per k step into one fp32
+//                      TMEM accumulator of BN columns; each slot is released by tcgen05.commit.
 //   warps 0-3          epilogue: thread r reads TMEM lane r (its row), rounds once to bf16, stages the
 //                      tile 128B-swizzled over the (then idle) ring, and one thread writes it with TMA
 //                      tensor stores; rows and columns past M and N are clipped by the tensor map, and
@@ -19,18 +19,22 @@
 namespace sk {
 namespace lin {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;  // CTA tile; one k step = one 128-byte swizzle row
-constexpr int kStages = 4;
+constexpr int kBM = 128, kBK = 64;  // tile rows; one k step = one 128-byte swizzle row
+constexpr int kStages = 4;  // deeper rings for the narrow tiles measured slower (one CTA per SM instead of two)
 constexpr int kThreads = 128;
-constexpr int A_BYTES = kBM * kBK * 2;                 // 16 KB
-constexpr int B_BYTES = kBN * kBK * 2;                 // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;         // 48 KB
-constexpr int OFF_BAR = kStages * STAGE_BYTES;         // full[kStages], empty[kStages], mma_done
-constexpr int NBAR = 2 * kStages + 1;
-constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
-constexpr int SMEM = OFF_TMEM + 16;
-static_assert(kBN / 64 * kBM * 128 <= OFF_BAR, "the output staging must fit over the ring");
-static_assert(SMEM <= 232448, "shared memory over the 227 KB per-CTA limit");
+
+template <int BN>
+struct Ly {
+  static constexpr int A_BYTES = kBM * kBK * 2;             // 16 KB
+  static constexpr int B_BYTES = BN * kBK * 2;              // 32, 16 or 8 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int OFF_BAR = kStages * STAGE_BYTES;     // full[kStages], empty[kStages], mma_done
+  static constexpr int NBAR = 2 * kStages + 1;
+  static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_TMEM + 16;
+  static_assert(BN / 64 * kBM * 128 <= OFF_BAR, "the output staging must fit over the ring");
+  static_assert(SMEM <= 232448, "shared memory over the 227 KB per-CTA limit");
+};
 
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
@@ -39,9 +43,12 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                : "memory");
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                   const __grid_constant__ CUtensorMap tmY, int N, int K, int* err) {
+  using L = Ly<BN>;
+  constexpr int A_BYTES = L::A_BYTES, STAGE_BYTES = L::STAGE_BYTES, OFF_BAR = L::OFF_BAR;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   if (sbase & 1023u) {  // uniform for the CTA, before any barrier: report and leave
@@ -51,9 +58,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* empty = full + kStages;
   uint64_t* mma_done = empty + kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_TMEM);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
   const int nk = (K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -70,7 +77,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmY);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kBN);
+    tmem_alloc(tmem_slot, BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -98,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&full[kc % kStages], (kc / kStages) & 1, err);
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- MMA issuer
-    constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN, 0, 0);
+    constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, 0, 0);
     for (int kc = 0; kc < nk; ++kc) {
       const int s = kc % kStages;
       if (!mbar_wait(&full[s], (kc / kStages) & 1, err)) break;
@@ -122,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
 #pragma unroll 1
-    for (int c = 0; c < kBN / 32; ++c) {
+    for (int c = 0; c < BN / 32; ++c) {
       float v[32];
       tmem_ld32(tmem + lane_off + c * 32, v);
       tmem_wait_ld();
@@ -148,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (ok && threadIdx.x == 0) {
 #pragma unroll
-    for (int c = 0; c < kBN / 64; ++c)  // column chunks that start inside y (the map clips the rest)
+    for (int c = 0; c < BN / 64; ++c)  // column chunks that start inside y (the map clips the rest)
       if (n0 + c * 64 < N) tma_store_3d(&tmY, smem + c * (kBM * 128), n0 + c * 64, m0, 0);
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -157,15 +164,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kBN);
+    tmem_dealloc(tmem, BN);
   }
+}
+
+
+template <int BN>
+static int launch(const void* x, const void* w, void* y, int M, int N, int K, int* err, int dev, void* stream) {
+  using L = Ly<BN>;
+  CUtensorMap mx, mw, my;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)M, 1};
+    cuuint64_t str[2] = {(cuuint64_t)K * 2, (cuuint64_t)M * K * 2};
+    cuuint32_t box[3] = {kBK, kBM, 1};
+    if (!sk_make_map_bf16(&mx, x, 3, dims, str, box)) return SK_ERR_CUDA;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)N, 1};
+    cuuint64_t str[2] = {(cuuint64_t)K * 2, (cuuint64_t)N * K * 2};
+    cuuint32_t box[3] = {kBK, BN, 1};
+    if (!sk_make_map_bf16(&mw, w, 3, dims, str, box)) return SK_ERR_CUDA;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, 1};
+    cuuint64_t str[2] = {(cuuint64_t)N * 2, (cuuint64_t)M * N * 2};
+    cuuint32_t box[3] = {64, kBM, 1};
+    if (!sk_make_map_bf16(&my, y, 3, dims, str, box)) return SK_ERR_CUDA;
+  }
+  static bool attr_done[64] = {};
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(linear_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM) != cudaSuccess)
+      return SK_ERR_CUDA;
+    attr_done[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((N + BN - 1) / BN), (unsigned)((M + kBM - 1) / kBM));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::SMEM;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = sk::kUsePdl ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, linear_kernel<BN>, mx, mw, my, N, K, err) != cudaSuccess) return SK_ERR_CUDA;
+  return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }
 
 }  // namespace lin
 }  // namespace sk
 
-extern "C" int sk_dit_linear(const void* x, const void* w, void* y, int M, int N, int K, int dtype, void* stream) {
+extern "C" int sk_dit_linear_ex(const void* x, const void* w, void* y, int M, int N, int K, int dtype, int tile_n,
+                                void* stream) {
   using namespace sk::lin;
+  if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256) return SK_ERR_INVALID_ARG;
   if (!x || !w || !y) return SK_ERR_INVALID_ARG;
   if (M <= 0 || N <= 0 || K <= 0) return SK_ERR_INVALID_ARG;
   if (dtype != SK_BF16) return SK_ERR_UNSUPPORTED;  // the fp32 mode keeps the library GEMM
@@ -177,43 +229,34 @@ extern "C" int sk_dit_linear(const void* x, const void* w, void* y, int M, int N
   if (rc != SK_OK) return rc;
   int* err = sk_error_word_ptr();
   if (!err) return SK_ERR_CUDA;
-  CUtensorMap mx, mw, my;
-  {
-    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)M, 1};
-    cuuint64_t str[2] = {(cuuint64_t)K * 2, (cuuint64_t)M * K * 2};
-    cuuint32_t box[3] = {kBK, kBM, 1};
-    if (!sk_make_map_bf16(&mx, x, 3, dims, str, box)) return SK_ERR_CUDA;
-  }
-  {
-    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)N, 1};
-    cuuint64_t str[2] = {(cuuint64_t)K * 2, (cuuint64_t)N * K * 2};
-    cuuint32_t box[3] = {kBK, kBN, 1};
-    if (!sk_make_map_bf16(&mw, w, 3, dims, str, box)) return SK_ERR_CUDA;
-  }
-  {
-    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, 1};
-    cuuint64_t str[2] = {(cuuint64_t)N * 2, (cuuint64_t)M * N * 2};
-    cuuint32_t box[3] = {64, kBM, 1};
-    if (!sk_make_map_bf16(&my, y, 3, dims, str, box)) return SK_ERR_CUDA;
-  }
-  static bool attr_done[64] = {};
+  // N tile: the fewest waves of CTAs weighted by a tile's relative cost (a 128 x 128 tile takes ~0.62
+  // and a 128 x 64 tile ~0.45 of a 128 x 256 one, the operand bytes per FLOP growing as BN shrinks)
+  static int sm_count[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
-      return SK_ERR_CUDA;
-    attr_done[dev] = true;
+  if (dev < 0 || dev >= 64) return SK_ERR_CUDA;
+  if (sm_count[dev] == 0 && cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return SK_ERR_CUDA;
+  const long long mt = (M + kBM - 1) / kBM;
+  int bn = tile_n ? tile_n : 256;
+  double best = 1e30;
+  if (tile_n == 0)
+  for (int cand : {256, 128, 64}) {
+    const long long tiles = mt * ((N + cand - 1) / cand);
+    const double waves = (double)((tiles + sm_count[dev] - 1) / sm_count[dev]);
+    const double cost = waves * (cand == 256 ? 1.0 : cand == 128 ? 0.62 : 0.45);
+    if (cost < best - 1e-9) {
+      best = cost;
+      bn = cand;
+    }
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = SMEM;
-  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = sk::kUsePdl ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, linear_kernel, mx, mw, my, N, K, err) != cudaSuccess) return SK_ERR_CUDA;
-  return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
+  switch (bn) {
+    case 256: return launch<256>(x, w, y, M, N, K, err, dev, stream);
+    case 128: return launch<128>(x, w, y, M, N, K, err, dev, stream);
+    default: return launch<64>(x, w, y, M, N, K, err, dev, stream);
+  }
+}
+
+extern "C" int sk_dit_linear(const void* x, const void* w, void* y, int M, int N, int K, int dtype, void* stream) {
+  return sk_dit_linear_ex(x, w, y, M, N, K, dtype, 0, stream);
 }

@@ -244,9 +244,10 @@ def dit_gate(y: torch.Tensor, o4: torch.Tensor, out: torch.Tensor | None = None,
     return out
 
 
-def dit_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def dit_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, tile_n: int = 0) -> torch.Tensor:
     """y = x · wᵀ (F.linear without bias, engine/fused.py:262-264) on the tcgen05 GEMM, bf16 in and out,
-    fp32 accumulation. x (M, K), w (N, K); returns (M, N)."""
+    fp32 accumulation. x (M, K), w (N, K); returns (M, N). tile_n: the CTA tile's width (64, 128, 256;
+    0 = chosen per call)."""
     _cuda_contig("x", x)
     _cuda_contig("w", w)
     _need(x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16, "dit_linear runs bf16 (fp32: use F.linear)")
@@ -258,8 +259,8 @@ def dit_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None
     _cuda_contig("out", out)
     _need(out.dtype == x.dtype and out.shape == (M, N), f"out must be ({M}, {N}) bf16")
     with _nvtx("sk_dit_linear"):
-        check(lib().sk_dit_linear(_ptr(x), _ptr(w), _ptr(out), M, N, K, _dtype_code(x.dtype), _stream()),
-              "sk_dit_linear")
+        check(lib().sk_dit_linear_ex(_ptr(x), _ptr(w), _ptr(out), M, N, K, _dtype_code(x.dtype), int(tile_n),
+                                     _stream()), "sk_dit_linear")
     return out
 
 

@@ -41,6 +41,21 @@ def test_linear_matches_oracle(cuda, M, N, K):
     assert rel_l2(got, lib) < 3e-3
 
 
+@pytest.mark.parametrize("tile_n", [64, 128, 256])
+@pytest.mark.parametrize("M,N,K", [(1536, 3072, 768), (97, 200, 72), (257, 1032, 4104), (640, 136, 520)])
+def test_linear_every_tile_width(cuda, tile_n, M, N, K):
+    g = torch.Generator().manual_seed(M + N * 3 + K + tile_n)
+    x = torch.randn(M, K, generator=g).bfloat16()
+    w = (torch.randn(N, K, generator=g) * K ** -0.5).bfloat16()
+    y = ops.dit_linear(x.to(cuda), w.to(cuda), tile_n=tile_n)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    err = rel_l2(y.float().cpu().numpy(), D.linear(x.float().numpy(), w.float().numpy(), "f32"))
+    assert err < 3e-3, err
+    auto = ops.dit_linear(x.to(cuda), w.to(cuda))
+    assert rel_l2(auto.float().cpu().numpy(), y.float().cpu().numpy()) < 1e-3
+
+
 def test_linear_graph_replay_and_stream(cuda):
     M, N, K = 640, 1024, 512
     g = torch.Generator().manual_seed(3)
@@ -76,3 +91,4 @@ def test_linear_errors(cuda):
     assert call(4, 4, 16, 1) == -2   # float32 unsupported
     assert call(0, 8, 16, 0) == -1   # empty
     assert call(4, 12, 16, 0) == -1  # N not a multiple of 8
+    assert _lib.lib().sk_dit_linear_ex(x.data_ptr(), x.data_ptr(), y.data_ptr(), 4, 8, 16, 0, 96, 0) == -1  # tile
