@@ -485,36 +485,59 @@ def layer_block(device, dist: Dist, calls: int = 120, sets: int = 4) -> dict:
 
 
 # ------------------------------------------------------------------------------------------- DiT GEMMs
-GEMM_SHAPES = (  # name, M (= B·L rows), N, K: the attention block's projections at B = 3, L = 512
-    ("c1_w_qkvg_b3", 1536, 4 * 768, 768), ("c1_w_o_b3", 1536, 768, 768),
-    ("c2_w_qkvg_b3", 1536, 4 * 2048, 2048), ("c2_w_o_b3", 1536, 2048, 2048),
+GEMM_SHAPES = (  # name, M (= B·L rows), N, K, fp8: the attention block's projections at B = 3, L = 512
+    ("c1_w_qkvg_b3", 1536, 4 * 768, 768, False), ("c1_w_o_b3", 1536, 768, 768, False),
+    ("c2_w_qkvg_b3", 1536, 4 * 2048, 2048, False), ("c2_w_o_b3", 1536, 2048, 2048, False),
+    ("c2_w_qkvg_b3_fp8", 1536, 4 * 2048, 2048, True), ("c2_w_o_b3_fp8", 1536, 2048, 2048, True),
 )
 
 
 def dit_gemm(device, dist: Dist, calls: int = 60, sets: int = 4) -> dict:
-    """The DiT projections y = x·wᵀ (engine/fused.py:262-264) on the tcgen05 GEMM (sk_dit_linear) and,
-    beside it, torch's F.linear (cuBLAS) on the same inputs; `sets` distinct (x, w) pairs rotated over
+    """The DiT projections y = x·wᵀ (engine/fused.py:262-264) on the tcgen05 GEMM (sk_dit_linear; the FP8
+    rows: sk_dit_linear_fp8, engine/fp8.py:87-89) and, beside it, torch's own GEMM on the same inputs
+    (F.linear / cuBLAS; torch._scaled_mm / cuBLASLt for FP8); `sets` distinct (x, w) pairs rotated over
     `calls` graph-replayed calls. Reports microseconds per call and TFLOP/s (2·M·N·K per call)."""
-    import torch.nn.functional as F
     from sokutou_b200 import ops
     out = {}
-    for name, M, N, K in GEMM_SHAPES:
+    for name, M, N, K, fp8 in GEMM_SHAPES:
         g = torch.Generator(device=device).manual_seed(9)
-        ins = [((torch.randn(M, K, device=device, generator=g)).bfloat16(),
-                (torch.randn(N, K, device=device, generator=g) * K ** -0.5).bfloat16(),
-                torch.empty(M, N, device=device, dtype=torch.bfloat16)) for _ in range(sets)]
-        res = {"M": M, "N": N, "K": K}
+        if fp8:
+            e4 = torch.float8_e4m3fn
+            ins = [((torch.randn(M, K, device=device, generator=g) * 8).to(e4),
+                    (torch.randn(N, K, device=device, generator=g) * 32).to(e4),
+                    torch.empty(M, N, device=device, dtype=torch.bfloat16)) for _ in range(sets)]
+            inv_x = torch.tensor([1 / 16], device=device)
+            inv_w = torch.tensor([1 / 64], device=device)
+        else:
+            ins = [((torch.randn(M, K, device=device, generator=g)).bfloat16(),
+                    (torch.randn(N, K, device=device, generator=g) * K ** -0.5).bfloat16(),
+                    torch.empty(M, N, device=device, dtype=torch.bfloat16)) for _ in range(sets)]
+        res = {"M": M, "N": N, "K": K, "dtype": "e4m3" if fp8 else "bf16"}
         for impl in ("sk", "cublas"):
-            if impl == "sk":
+            if impl == "sk" and fp8:
+                run = lambda: [ops.dit_linear_fp8(ins[i % sets][0], ins[i % sets][1], inv_x, inv_w, out=ins[i % sets][2])
+                               for i in range(calls)]
+            elif impl == "sk":
                 run = lambda: [ops.dit_linear(ins[i % sets][0], ins[i % sets][1], out=ins[i % sets][2])
                                for i in range(calls)]
+            elif fp8:
+                run = lambda: [torch._scaled_mm(ins[i % sets][0], ins[i % sets][1].t(), inv_x, inv_w,
+                                                out_dtype=torch.bfloat16, out=ins[i % sets][2]) for i in range(calls)]
             else:
                 run = lambda: [torch.matmul(ins[i % sets][0], ins[i % sets][1].t(), out=ins[i % sets][2])
                                for i in range(calls)]
             st = torch.cuda.Stream(device)
             st.wait_stream(torch.cuda.current_stream(device))
             with torch.cuda.stream(st):
-                run()
+                try:
+                    run()
+                except RuntimeError as e:  # torch's FP8 GEMM may not take this shape or build (same on every rank)
+                    if impl == "sk":
+                        raise
+                    res["cublas_us"] = None
+                    res["cublas_error"] = str(e).splitlines()[0][:160]
+                    torch.cuda.current_stream(device).wait_stream(st)
+                    continue
             torch.cuda.current_stream(device).wait_stream(st)
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr):

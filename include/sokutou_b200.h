@@ -176,6 +176,20 @@ SK_API int sk_dit_linear(const void* x, const void* w, void* y, int M, int N, in
 SK_API int sk_dit_linear_ex(const void* x, const void* w, void* y, int M, int N, int K, int dtype, int tile_n,
                             void* stream);
 
+/*
+ * The FP8 projection of the engine's FP8 path (engine/fp8.py:87-89, torch._scaled_mm):
+ * y = (x8 · w8ᵀ) · inv_scale_x · inv_scale_w, fp32 accumulation, rounded once to bf16.
+ *
+ *   x8          : (M, K) e4m3 bytes (the activation, written by sk_dit_gate with SK_E4M3 for w_o)
+ *   w8          : (N, K) e4m3 bytes (the weight times its power-of-two scale)
+ *   y           : (M, N) bf16
+ *   inv_scale_x, inv_scale_w : device fp32 scalars, read by the kernel (set before graph capture)
+ *   tile_n      : 0 (chosen per call), 64, 128 or 256
+ *   K a multiple of 16, N a multiple of 8, pointers 16-byte aligned.
+ */
+SK_API int sk_dit_linear_fp8(const void* x8, const void* w8, void* y, const float* inv_scale_x,
+                             const float* inv_scale_w, int M, int N, int K, int tile_n, void* stream);
+
 /* ---- 2. Qwen3 talker decode attention --------------------------------------------------------- */
 
 /* Bytes of scratch sk_decode_attention needs for a cache of max_len positions. */

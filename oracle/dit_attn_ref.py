@@ -196,6 +196,16 @@ def linear(x, w, out: str = "f32") -> np.ndarray:
     return bf16_round(y) if out == "bf16" else y
 
 
+def linear_fp8(x8, w8, inv_scale_x: float, inv_scale_w: float) -> np.ndarray:
+    """torch._scaled_mm(x8, w8.t(), inv_x, inv_w, out_dtype=bf16) (engine/fp8.py:87-89): the e4m3 codes
+    x8 (M, K) and w8 (N, K) decoded exactly, multiplied in float64, times inv_x · inv_w (float32),
+    rounded once to bf16 (returned as float32)."""
+    x = e4m3_decode(np.asarray(x8, np.uint8)).astype(np.float64)
+    w = e4m3_decode(np.asarray(w8, np.uint8)).astype(np.float64)
+    s = np.float64(np.float32(inv_scale_x) * np.float32(inv_scale_w))
+    return bf16_round((x @ w.T * s).astype(np.float32))
+
+
 def gate(y, o4, out: str = "f32", out_scale: float = 1.0) -> np.ndarray:
     """out[r, c] = y[r, c] · (1 / (1 + exp(-o4[r, 3D + c]))) in float32 (engine/fused.py:182-190),
     then rounded once: out = "f32" (as is), "bf16" (round to nearest even, returned as float32) or

@@ -31,6 +31,7 @@ SIGNATURES = {
     "sk_dit_gate": (_I, [_P, _P, _P, _LL, _I, _I, _I, _F, _P]),
     "sk_dit_linear": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "sk_dit_linear_ex": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "sk_dit_linear_fp8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "sk_dit_attention_layer": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _LL, _LL, _F, _I,
                                     _F, _P]),
     "sk_decode_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),

@@ -13,20 +13,23 @@
 //                      tile 128B-swizzled over the (then idle) ring, and one thread writes it with TMA
 //                      tensor stores; rows and columns past M and N are clipped by the tensor map, and
 //                      k past K reads zeros.
+// FP8 = true: the engine's FP8 projections (engine/fp8.py: torch._scaled_mm on e4m3 activations and
+// e4m3 weights, each with a per-tensor inverse scale, bf16 out): kind::f8f6f4 MMAs (K 32) on 128-wide
+// k steps of bytes, and the epilogue multiplies the fp32 sum by inv_x · inv_w before the bf16 rounding.
 // Every wait gives up after 2 s (error word, then the CTA unwinds). No TMA multicast.
 #include "sk_common.cuh"
 
 namespace sk {
 namespace lin {
 
-constexpr int kBM = 128, kBK = 64;  // tile rows; one k step = one 128-byte swizzle row
+constexpr int kBM = 128;  // tile rows; one k step = one 128-byte swizzle row (64 bf16 or 128 e4m3)
 constexpr int kStages = 4;  // deeper rings for the narrow tiles measured slower (one CTA per SM instead of two)
 constexpr int kThreads = 128;
 
 template <int BN>
 struct Ly {
-  static constexpr int A_BYTES = kBM * kBK * 2;             // 16 KB
-  static constexpr int B_BYTES = BN * kBK * 2;              // 32, 16 or 8 KB
+  static constexpr int A_BYTES = kBM * 128;                 // 16 KB
+  static constexpr int B_BYTES = BN * 128;                  // 32, 16 or 8 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int OFF_BAR = kStages * STAGE_BYTES;     // full[kStages], empty[kStages], mma_done
   static constexpr int NBAR = 2 * kStages + 1;
@@ -43,10 +46,12 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                : "memory");
 }
 
-template <int BN>
+template <int BN, bool FP8>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                  const __grid_constant__ CUtensorMap tmY, int N, int K, int* err) {
+                  const __grid_constant__ CUtensorMap tmY, int N, int K, const float* inv_x, const float* inv_w,
+                  int* err) {
+  constexpr int kBK = FP8 ? 128 : 64;  // elements per k step
   using L = Ly<BN>;
   constexpr int A_BYTES = L::A_BYTES, STAGE_BYTES = L::STAGE_BYTES, OFF_BAR = L::OFF_BAR;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -105,16 +110,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&full[kc % kStages], (kc / kStages) & 1, err);
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- MMA issuer
-    constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, 0, 0);
+    constexpr uint32_t idesc = FP8 ? idesc_e4m3_f32(kBM, BN) : idesc_bf16_f32(kBM, BN, 0, 0);
     for (int kc = 0; kc < nk; ++kc) {
       const int s = kc % kStages;
       if (!mbar_wait(&full[s], (kc / kStages) & 1, err)) break;
       tc_fence_after();
       const uint32_t a = sbase + s * STAGE_BYTES, bw = a + A_BYTES;
 #pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk)
-        tc_mma_ss(tmem, smem_desc_sw128(a + kk * 32, 16, 1024), smem_desc_sw128(bw + kk * 32, 16, 1024), idesc,
-                  (kc > 0 || kk > 0) ? 1u : 0u);
+      for (int kk = 0; kk < 4; ++kk) {  // 32 bytes of K per instruction: 16 bf16 or 32 e4m3
+        const uint64_t da = smem_desc_sw128(a + kk * 32, 16, 1024), db = smem_desc_sw128(bw + kk * 32, 16, 1024);
+        if constexpr (FP8)
+          tc_mma_ss_f8(tmem, da, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+        else
+          tc_mma_ss(tmem, da, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+      }
       tc_commit(&empty[s]);  // the slot is free once these MMAs have read it
     }
     tc_commit(mma_done);  // every MMA issued has completed
@@ -125,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool ok = mbar_wait(mma_done, 0, err);
   ok = __all_sync(0xffffffffu, ok);
   const int row = threadIdx.x;  // TMEM lane == row of the tile
+  const float oscale = FP8 ? __ldg(inv_x) * __ldg(inv_w) : 1.f;  // the two inverse scales, set before capture
   if (ok) {
     tc_fence_after();
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
@@ -140,7 +150,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]);
+          const float v0 = FP8 ? v[8 * u + 2 * e] * oscale : v[8 * u + 2 * e];
+          const float v1 = FP8 ? v[8 * u + 2 * e + 1] * oscale : v[8 * u + 2 * e + 1];
+          const __nv_bfloat162 b2 = __floats2bfloat162_rn(v0, v1);
           pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
         }
         const int unit = (c & 1) * 4 + u;
@@ -169,21 +181,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
-template <int BN>
-static int launch(const void* x, const void* w, void* y, int M, int N, int K, int* err, int dev, void* stream) {
+template <int BN, bool FP8>
+static int launch(const void* x, const void* w, void* y, int M, int N, int K, const float* inv_x, const float* inv_w,
+                  int* err, int dev, void* stream) {
   using L = Ly<BN>;
+  constexpr int kBK = FP8 ? 128 : 64;
+  constexpr cuuint64_t es = FP8 ? 1 : 2;  // operand bytes per element
+  const CUtensorMapDataType dt = FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap mx, mw, my;
   {
     cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)M, 1};
-    cuuint64_t str[2] = {(cuuint64_t)K * 2, (cuuint64_t)M * K * 2};
+    cuuint64_t str[2] = {(cuuint64_t)K * es, (cuuint64_t)M * K * es};
     cuuint32_t box[3] = {kBK, kBM, 1};
-    if (!sk_make_map_bf16(&mx, x, 3, dims, str, box)) return SK_ERR_CUDA;
+    if (!sk_make_map_sw128(&mx, dt, x, 3, dims, str, box)) return SK_ERR_CUDA;
   }
   {
     cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)N, 1};
-    cuuint64_t str[2] = {(cuuint64_t)K * 2, (cuuint64_t)N * K * 2};
+    cuuint64_t str[2] = {(cuuint64_t)K * es, (cuuint64_t)N * K * es};
     cuuint32_t box[3] = {kBK, BN, 1};
-    if (!sk_make_map_bf16(&mw, w, 3, dims, str, box)) return SK_ERR_CUDA;
+    if (!sk_make_map_sw128(&mw, dt, w, 3, dims, str, box)) return SK_ERR_CUDA;
   }
   {
     cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, 1};
@@ -193,7 +209,8 @@ static int launch(const void* x, const void* w, void* y, int M, int N, int K, in
   }
   static bool attr_done[64] = {};
   if (!attr_done[dev]) {
-    if (cudaFuncSetAttribute(linear_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(linear_kernel<BN, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM) !=
+        cudaSuccess)
       return SK_ERR_CUDA;
     attr_done[dev] = true;
   }
@@ -207,40 +224,25 @@ static int launch(const void* x, const void* w, void* y, int M, int N, int K, in
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = sk::kUsePdl ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, linear_kernel<BN>, mx, mw, my, N, K, err) != cudaSuccess) return SK_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, linear_kernel<BN, FP8>, mx, mw, my, N, K, inv_x, inv_w, err) != cudaSuccess)
+    return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }
 
 }  // namespace lin
 }  // namespace sk
 
-extern "C" int sk_dit_linear_ex(const void* x, const void* w, void* y, int M, int N, int K, int dtype, int tile_n,
-                                void* stream) {
-  using namespace sk::lin;
-  if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256) return SK_ERR_INVALID_ARG;
-  if (!x || !w || !y) return SK_ERR_INVALID_ARG;
-  if (M <= 0 || N <= 0 || K <= 0) return SK_ERR_INVALID_ARG;
-  if (dtype != SK_BF16) return SK_ERR_UNSUPPORTED;  // the fp32 mode keeps the library GEMM
-  // tensor maps: 16-byte aligned bases and row strides
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15)
-    return SK_ERR_INVALID_ARG;
-  if (K % 8 || N % 8) return SK_ERR_INVALID_ARG;
-  const int rc = sk_check_device();
-  if (rc != SK_OK) return rc;
-  int* err = sk_error_word_ptr();
-  if (!err) return SK_ERR_CUDA;
-  // N tile: the fewest waves of CTAs weighted by a tile's relative cost (a 128 x 128 tile takes ~0.62
-  // and a 128 x 64 tile ~0.45 of a 128 x 256 one, the operand bytes per FLOP growing as BN shrinks)
+namespace sk {
+namespace lin {
+// N tile: the fewest waves of CTAs weighted by a tile's relative cost (a 128 x 128 tile takes ~0.62
+// and a 128 x 64 tile ~0.45 of a 128 x 256 one, the operand bytes per FLOP growing as BN shrinks)
+static int pick_tile(int M, int N, int dev) {
   static int sm_count[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return SK_ERR_CUDA;
   if (sm_count[dev] == 0 && cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return SK_ERR_CUDA;
+    return 0;
   const long long mt = (M + kBM - 1) / kBM;
-  int bn = tile_n ? tile_n : 256;
+  int bn = 256;
   double best = 1e30;
-  if (tile_n == 0)
   for (int cand : {256, 128, 64}) {
     const long long tiles = mt * ((N + cand - 1) / cand);
     const double waves = (double)((tiles + sm_count[dev] - 1) / sm_count[dev]);
@@ -250,11 +252,47 @@ extern "C" int sk_dit_linear_ex(const void* x, const void* w, void* y, int M, in
       bn = cand;
     }
   }
+  return bn;
+}
+
+template <bool FP8>
+static int run(const void* x, const void* w, void* y, const float* inv_x, const float* inv_w, int M, int N, int K,
+               int tile_n, void* stream) {
+  if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256) return SK_ERR_INVALID_ARG;
+  if (!x || !w || !y) return SK_ERR_INVALID_ARG;
+  if (M <= 0 || N <= 0 || K <= 0) return SK_ERR_INVALID_ARG;
+  if (FP8 && (!inv_x || !inv_w)) return SK_ERR_INVALID_ARG;
+  // tensor maps: 16-byte aligned bases and row strides
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15)
+    return SK_ERR_INVALID_ARG;
+  if (K % (FP8 ? 16 : 8) || N % 8) return SK_ERR_INVALID_ARG;
+  const int rc = sk_check_device();
+  if (rc != SK_OK) return rc;
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return SK_ERR_CUDA;
+  const int bn = tile_n ? tile_n : pick_tile(M, N, dev);
   switch (bn) {
-    case 256: return launch<256>(x, w, y, M, N, K, err, dev, stream);
-    case 128: return launch<128>(x, w, y, M, N, K, err, dev, stream);
-    default: return launch<64>(x, w, y, M, N, K, err, dev, stream);
+    case 256: return launch<256, FP8>(x, w, y, M, N, K, inv_x, inv_w, err, dev, stream);
+    case 128: return launch<128, FP8>(x, w, y, M, N, K, inv_x, inv_w, err, dev, stream);
+    case 64: return launch<64, FP8>(x, w, y, M, N, K, inv_x, inv_w, err, dev, stream);
+    default: return SK_ERR_CUDA;
   }
+}
+}  // namespace lin
+}  // namespace sk
+
+extern "C" int sk_dit_linear_ex(const void* x, const void* w, void* y, int M, int N, int K, int dtype, int tile_n,
+                                void* stream) {
+  if (dtype != SK_BF16) return SK_ERR_UNSUPPORTED;  // the fp32 mode keeps the library GEMM
+  return sk::lin::run<false>(x, w, y, nullptr, nullptr, M, N, K, tile_n, stream);
+}
+
+extern "C" int sk_dit_linear_fp8(const void* x8, const void* w8, void* y, const float* inv_scale_x,
+                                 const float* inv_scale_w, int M, int N, int K, int tile_n, void* stream) {
+  return sk::lin::run<true>(x8, w8, y, inv_scale_x, inv_scale_w, M, N, K, tile_n, stream);
 }
 
 extern "C" int sk_dit_linear(const void* x, const void* w, void* y, int M, int N, int K, int dtype, void* stream) {

@@ -264,6 +264,31 @@ def dit_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None
     return out
 
 
+def dit_linear_fp8(x8: torch.Tensor, w8: torch.Tensor, inv_scale_x: torch.Tensor, inv_scale_w: torch.Tensor,
+                   out: torch.Tensor | None = None, tile_n: int = 0) -> torch.Tensor:
+    """y = (x8 · w8ᵀ) · inv_scale_x · inv_scale_w in bf16 — torch._scaled_mm(x8, w8.t(), inv_x, inv_w,
+    out_dtype=bf16) of engine/fp8.py:87-89 on the tcgen05 kind::f8f6f4 GEMM. x8 (M, K) and w8 (N, K) are
+    e4m3 tensors (torch.float8_e4m3fn, or their raw bytes as torch.uint8); the scales are one-element
+    fp32 device tensors."""
+    for name, t in (("x8", x8), ("w8", w8)):
+        _cuda_contig(name, t)
+        _need(t.element_size() == 1 and t.dim() == 2, f"{name} must be 2-D e4m3 (or uint8) bytes")
+    for name, t in (("inv_scale_x", inv_scale_x), ("inv_scale_w", inv_scale_w)):
+        _cuda_contig(name, t)
+        _need(t.dtype == torch.float32 and t.numel() == 1, f"{name} must be one fp32 element")
+    _need(x8.shape[1] == w8.shape[1], "x8 must be (M, K) and w8 (N, K)")
+    M, K = x8.shape
+    N = w8.shape[0]
+    if out is None:
+        out = torch.empty((M, N), device=x8.device, dtype=torch.bfloat16)
+    _cuda_contig("out", out)
+    _need(out.dtype == torch.bfloat16 and out.shape == (M, N), f"out must be ({M}, {N}) bf16")
+    with _nvtx("sk_dit_linear_fp8"):
+        check(lib().sk_dit_linear_fp8(_ptr(x8), _ptr(w8), _ptr(out), _ptr(inv_scale_x), _ptr(inv_scale_w), M, N, K,
+                                      int(tile_n), _stream()), "sk_dit_linear_fp8")
+    return out
+
+
 def decode_workspace_bytes(max_len: int, nq: int, nkv: int, hd: int = 128, cache_dtype: torch.dtype = torch.bfloat16) -> int:
     return int(lib().sk_decode_workspace_bytes(max_len, nq, nkv, hd, _dtype_code(cache_dtype)))
 

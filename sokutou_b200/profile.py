@@ -41,6 +41,8 @@ CASES = {
     "linear_c1_qkvg_b3": ("linear", (1536, 3072, 768), "sk"), "cublas_c1_qkvg_b3": ("linear", (1536, 3072, 768), "cublas"),
     "linear_c2_qkvg_b3": ("linear", (1536, 8192, 2048), "sk"), "cublas_c2_qkvg_b3": ("linear", (1536, 8192, 2048), "cublas"),
     "linear_c2_o_b3": ("linear", (1536, 2048, 2048), "sk"), "cublas_c2_o_b3": ("linear", (1536, 2048, 2048), "cublas"),
+    "linear_fp8_c2_qkvg_b3": ("linear", (1536, 8192, 2048), "sk_fp8"),
+    "scaledmm_c2_qkvg_b3": ("linear", (1536, 8192, 2048), "cublas_fp8"),
     # calibration: what a chain of dependent kernels costs on this GPU without any attention work
     "calib_tiny": ("calib", 0, None), "calib_copy_4.6MB": ("calib", 4616192, None),
 }
@@ -136,10 +138,21 @@ def linear_case(mnk, impl, sets, dev):
     M, N, K = mnk
     g = torch.Generator(device=dev).manual_seed(0)
     fns = []
+    inv_x = torch.tensor([1 / 16], device=dev)
+    inv_w = torch.tensor([1 / 64], device=dev)
     for _ in range(sets):
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        if impl.endswith("fp8"):  # the FP8 path (engine/fp8.py:87-89): e4m3 operands, per-tensor inverse scales
+            x = (torch.randn(M, K, device=dev, generator=g) * 8).to(torch.float8_e4m3fn)
+            w = (torch.randn(N, K, device=dev, generator=g) * 32).to(torch.float8_e4m3fn)
+            if impl == "sk_fp8":
+                fns.append(lambda x=x, w=w, y=y: ops.dit_linear_fp8(x, w, inv_x, inv_w, out=y))
+            else:
+                fns.append(lambda x=x, w=w, y=y: torch._scaled_mm(x, w.t(), inv_x, inv_w, out_dtype=torch.bfloat16,
+                                                                  out=y))
+            continue
         x = torch.randn(M, K, device=dev, generator=g).bfloat16()
         w = (torch.randn(N, K, device=dev, generator=g) * K ** -0.5).bfloat16()
-        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         if impl == "sk":
             fns.append(lambda x=x, w=w, y=y: ops.dit_linear(x, w, out=y))
         else:

@@ -92,3 +92,53 @@ def test_linear_errors(cuda):
     assert call(0, 8, 16, 0) == -1   # empty
     assert call(4, 12, 16, 0) == -1  # N not a multiple of 8
     assert _lib.lib().sk_dit_linear_ex(x.data_ptr(), x.data_ptr(), y.data_ptr(), 4, 8, 16, 0, 96, 0) == -1  # tile
+
+
+def _e4m3_operands(M, N, K, seed):
+    rng = np.random.default_rng(seed)
+    x8 = D.e4m3_encode((rng.standard_normal((M, K)) * 8).astype(np.float32))
+    w8 = D.e4m3_encode((rng.standard_normal((N, K)) * 32).astype(np.float32))
+    return x8, w8
+
+
+@pytest.mark.parametrize("M,N,K,tile_n", [(1536, 3072, 768, 0), (1536, 8192, 2048, 0), (97, 200, 80, 0),
+                                          (130, 264, 144, 64), (130, 264, 144, 128), (130, 264, 144, 256),
+                                          (1, 8, 16, 0), (257, 1032, 4112, 0)])
+def test_linear_fp8_matches_oracle(cuda, M, N, K, tile_n):
+    """The FP8 projection (torch._scaled_mm at engine/fp8.py:87-89) against the oracle's exact decode of
+    the same e4m3 codes: relative L2 <= 3e-3 (one bf16 rounding); and against torch's own _scaled_mm."""
+    x8, w8 = _e4m3_operands(M, N, K, M + N + K)
+    inv_x = torch.tensor([1 / 16], device=cuda)
+    inv_w = torch.tensor([1 / 64], device=cuda)
+    xt = torch.from_numpy(x8).to(cuda)
+    wt = torch.from_numpy(w8).to(cuda)
+    buf = torch.full((M * N + 4096,), 3.0, dtype=torch.bfloat16, device=cuda)
+    y = ops.dit_linear_fp8(xt, wt, inv_x, inv_w, out=buf[:M * N].view(M, N), tile_n=tile_n)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.all(buf[M * N:] == 3.0)
+    got = y.float().cpu().numpy()
+    want = D.linear_fp8(x8, w8, 1 / 16, 1 / 64)
+    err = rel_l2(got, want)
+    assert err < 3e-3, err
+    if K % 16 == 0 and N % 16 == 0 and hasattr(torch, "_scaled_mm"):
+        try:
+            lib = torch._scaled_mm(xt.view(torch.float8_e4m3fn), wt.view(torch.float8_e4m3fn).t(), inv_x, inv_w,
+                                   out_dtype=torch.bfloat16)
+        except RuntimeError:  # a shape or build torch's FP8 GEMM does not take
+            lib = None
+        if lib is not None:
+            assert rel_l2(got, lib.float().cpu().numpy()) < 3e-3
+
+
+def test_linear_fp8_errors(cuda):
+    x = torch.zeros(4, 24, device=cuda, dtype=torch.uint8)
+    w = torch.zeros(8, 24, device=cuda, dtype=torch.uint8)
+    one = torch.ones(1, device=cuda)
+    with pytest.raises(SokutouError):
+        ops.dit_linear_fp8(x, w, one, one)  # K = 24 is not a multiple of 16
+    from sokutou_b200 import _lib
+    x = torch.zeros(4, 32, device=cuda, dtype=torch.uint8)
+    y = torch.zeros(4, 8, device=cuda, dtype=torch.bfloat16)
+    assert _lib.lib().sk_dit_linear_fp8(x.data_ptr(), x.data_ptr(), y.data_ptr(), 0, one.data_ptr(), 4, 8, 32, 0,
+                                        0) == -1  # missing scale
