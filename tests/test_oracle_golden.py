@@ -123,3 +123,34 @@ def test_attention_layer_oracle_matches_reference(case):
             g["bias3"])
     assert rel_l2(D.attention_layer(*args, bf16=False), g["gated"]) < FP32_TOL
     assert rel_l2(D.attention_layer(*args, bf16=True), g["gated"]) < 1e-2
+
+
+def test_linear_matches_torch_linear():
+    """The projection restatement against torch's own F.linear (the reference's `mm`,
+    engine/fused.py:262-264) in float64 on the host."""
+    import torch
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((37, 72)).astype(np.float32)
+    w = rng.standard_normal((40, 72)).astype(np.float32)
+    want = torch.nn.functional.linear(torch.from_numpy(x).double(), torch.from_numpy(w).double()).numpy()
+    assert rel_l2(D.linear(x, w, "f32"), want) < 1e-7
+    got = D.linear(x, w, "bf16")
+    ref = torch.from_numpy(want.astype(np.float32)).bfloat16().float().numpy()
+    assert np.array_equal(got, ref)
+
+
+def test_e4m3_decode_matches_torch_float8():
+    """Every finite e4m3 code decodes to the value torch's float8_e4m3fn gives it (the operand type of
+    torch._scaled_mm at engine/fp8.py:87-89), and linear_fp8 equals the float64 product of those values."""
+    import torch
+    codes = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], np.uint8)
+    mine = D.e4m3_decode(codes)
+    theirs = torch.from_numpy(codes).view(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(mine, theirs)
+    rng = np.random.default_rng(5)
+    x8 = rng.choice(codes, size=(9, 32))
+    w8 = rng.choice(codes, size=(16, 32))
+    xs = torch.from_numpy(x8).view(torch.float8_e4m3fn).double()
+    ws = torch.from_numpy(w8).view(torch.float8_e4m3fn).double()
+    want = ((xs @ ws.T) * (np.float32(1 / 16) * np.float32(1 / 64))).float().bfloat16().float().numpy()
+    assert np.array_equal(D.linear_fp8(x8, w8, 1 / 16, 1 / 64), want)
