@@ -22,6 +22,7 @@ bounded sample of the same workload and prints the same line with "impl": "refer
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -51,22 +52,50 @@ def peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic(name: str):
-    """DRAM bytes per launch recorded by an ncu capture summary in profiles/<name> ('traffic_bytes_per_launch: N')."""
+WORKLOAD = ("BASELINE config 1: DiT attention, full synthesis (12 layers x 20 steps, CFG B=3 on 10 steps, "
+            "B=1 on 10) for L in 128/256/512")
+
+
+def c1_config(world: int, calls: int, flops: int) -> dict:
+    """The headline workload, identical in both arms' JSON lines."""
+    return {"workload": WORKLOAD, "heads": 12, "head_dim": 64, "text_keys": 64, "speaker_keys": 192,
+            "calls_per_step": calls, "flops_per_step": flops, "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (distinct q/k/v per call, ~3 GB per step)"}
+
+
+def profile_traffic_mix(name: str, shapes):
+    """DRAM bytes per launch averaged over the step's call mix, from the per-shape lines
+    'traffic_bytes_per_launch <shape>_b<B>: N' of an ncu summary in profiles/<name> (one launch of each
+    shape captured with dram__bytes_read.sum and dram__bytes_write.sum). None if a shape is missing."""
     p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
         return None
+    per = {}
     for line in open(p):
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        t = line.strip()
+        if t.startswith("traffic_bytes_per_launch ") and ":" in t:
+            key, val = t[len("traffic_bytes_per_launch "):].split(":", 1)
             try:
-                return float(line.split(":", 1)[1].split()[0])
+                per[key.strip()] = float(val.split()[0])
             except ValueError:
+                pass
+    tot = n = 0
+    for sh in shapes:
+        for B in sh.synthesis_calls():
+            key = f"{sh.name}_b{B}"
+            if key not in per:
                 return None
-    return None
+            tot += per[key]
+            n += 1
+    return round(tot / n) if n else None
 
 
 # ---------------------------------------------------------------------------------------------- dist
 class Dist:
+    """One process per GPU under torchrun. The ranks share no data (request-parallel, no collectives on
+    the data path); the process group exists only to line the ranks up around the timed region and to
+    take the max / sum of the timing scalars, so it is gloo over host scalars, not NCCL."""
+
     def __init__(self, gpus: int):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
@@ -77,8 +106,7 @@ class Dist:
 
             import torch.distributed as dist
             torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local))
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
             self.pg = dist
         self.device = torch.device("cuda", self.local)
 
@@ -86,19 +114,16 @@ class Dist:
         if self.pg:
             self.pg.barrier()
 
-    def max(self, x: float) -> float:
-        if not self.pg:
-            return x
-        t = torch.tensor([x], device=self.device, dtype=torch.float64)
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+    def _reduce(self, x: float, op) -> float:
+        t = torch.tensor([x], dtype=torch.float64)
+        self.pg.all_reduce(t, op=op)
         return float(t.item())
 
+    def max(self, x: float) -> float:
+        return self._reduce(x, self.pg.ReduceOp.MAX) if self.pg else x
+
     def sum(self, x: float) -> float:
-        if not self.pg:
-            return x
-        t = torch.tensor([x], device=self.device, dtype=torch.float64)
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
-        return float(t.item())
+        return self._reduce(x, self.pg.ReduceOp.SUM) if self.pg else x
 
     def close(self):
         if self.pg:
@@ -294,8 +319,12 @@ def time_graphs(graphs, steps: int, warmup: int, dist: Dist, label: str = "timed
     return dist.max(e0.elapsed_time(e1))
 
 
-def dit_e2e(syn: list, steps: int, warmup: int, dist: Dist, device):
-    """Every call through the public op with pinned host inputs/outputs (h2d + kernel + d2h)."""
+def dit_e2e(syn: list, steps: int, warmup: int, dist: Dist, device, depth: int = 3):
+    """Every call through the public op (ops.dit_attention, C ABI) with pinned host inputs and outputs:
+    each call's q/k/v copied host->device and its y copied back, all inside the timed region. Three
+    streams pipeline the calls: the inputs of call i+1 go up (copy-in stream) and the output of call i-1
+    comes back (copy-out stream) while call i computes, through a ring of `depth` device buffer sets
+    guarded by events — H2D and D2H use separate copy engines and overlap the kernels."""
     from sokutou_b200 import ops
     hosts = []
     for s in syn:
@@ -304,27 +333,60 @@ def dit_e2e(syn: list, steps: int, warmup: int, dist: Dist, device):
         hy = torch.empty(s.y[0].shape, dtype=torch.bfloat16).pin_memory()
         hctx = [(k.cpu().pin_memory(), v.cpu().pin_memory()) for k, v in s.ctx]
         hb = s.bias.cpu().pin_memory()
-        hosts.append((hq, hk, hv, hy, hctx, hb))
+        ring = [tuple(torch.empty_like(t[0]) for t in (s.q, s.k, s.v, s.y)) for _ in range(depth)]
+        dctx = [(torch.empty_like(k), torch.empty_like(v)) for k, v in s.ctx]
+        hosts.append((hq, hk, hv, hy, hctx, hb, ring, dctx, torch.empty_like(s.bias)))
+    s_in, s_cmp, s_out = (torch.cuda.Stream(device) for _ in range(3))
+    ev = lambda: torch.cuda.Event()
     h2d = d2h = 0
 
     def one_step(count):
         nonlocal h2d, d2h
-        for s, (hq, hk, hv, hy, hctx, hb) in zip(syn, hosts):
+        for s, (hq, hk, hv, hy, hctx, hb, ring, dctx, dbias) in zip(syn, hosts):
             nl = s.shape.n_layers
-            bias = hb.to(device, non_blocking=True)
-            ctx = [(k.to(device, non_blocking=True), v.to(device, non_blocking=True)) for k, v in hctx]
+            with torch.cuda.stream(s_in):  # the synthesis' conditioning keys and mask, once
+                s_in.wait_stream(s_cmp)
+                dbias.copy_(hb, non_blocking=True)
+                for (dk, dv), (k, v) in zip(dctx, hctx):
+                    dk.copy_(k, non_blocking=True)
+                    dv.copy_(v, non_blocking=True)
             if count:
                 h2d += hb.numel() * 2 + sum(k.numel() * 2 + v.numel() * 2 for k, v in hctx)
+            free_in = [None] * depth   # the kernel that last read slot r's q/k/v
+            free_out = [None] * depth  # the copy that last read slot r's y
             for i, B in enumerate(s.calls):
-                q = hq[:B].to(device, non_blocking=True)
-                k = hk[:B].to(device, non_blocking=True)
-                v = hv[:B].to(device, non_blocking=True)
-                kc, vc = ctx[i % nl]
-                y = ops.dit_attention(q, k, v, kc, vc, bias[:B])
-                hy[:B].copy_(y, non_blocking=True)
+                r = i % depth
+                q, k, v, y = (t[:B] for t in ring[r])
+                with torch.cuda.stream(s_in):
+                    if free_in[r] is not None:
+                        s_in.wait_event(free_in[r])
+                    q.copy_(hq[:B], non_blocking=True)
+                    k.copy_(hk[:B], non_blocking=True)
+                    v.copy_(hv[:B], non_blocking=True)
+                    landed = ev()
+                    landed.record(s_in)
+                with torch.cuda.stream(s_cmp):
+                    s_cmp.wait_event(landed)
+                    if free_out[r] is not None:
+                        s_cmp.wait_event(free_out[r])
+                    kc, vc = dctx[i % nl]
+                    ops.dit_attention(q, k, v, kc, vc, dbias[:B], out=y)
+                    done = ev()
+                    done.record(s_cmp)
+                    free_in[r] = done
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(done)
+                    hy[:B].copy_(y, non_blocking=True)
+                    back = ev()
+                    back.record(s_out)
+                    free_out[r] = back
                 if count:
                     h2d += 3 * q.numel() * 2
                     d2h += y.numel() * 2
+            for st in (s_in, s_cmp, s_out):  # the next synthesis reuses the ring and the ctx buffers
+                torch.cuda.current_stream(device).wait_stream(st)
+            for st in (s_in, s_cmp, s_out):
+                st.wait_stream(torch.cuda.current_stream(device))
 
     for _ in range(warmup):
         one_step(False)
@@ -332,10 +394,15 @@ def dit_e2e(syn: list, steps: int, warmup: int, dist: Dist, device):
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    cur = torch.cuda.current_stream(device)
+    e0.record(cur)
+    for st in (s_in, s_cmp, s_out):
+        st.wait_stream(cur)
     for _ in range(steps):
         one_step(True)
-    e1.record()
+    for st in (s_in, s_cmp, s_out):
+        cur.wait_stream(st)
+    e1.record(cur)
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
@@ -481,6 +548,103 @@ def layer_block(device, dist: Dist, calls: int = 120, sets: int = 4) -> dict:
         res["speedup"] = round(res["separate_us"] / res["fused_us"], 3)
         out[name] = res
     torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------------------ reference op on the GPU
+def sdpa_gpu(device, dist: Dist, calls: int = 96, min_pool_bytes: int = 384 << 20) -> dict:
+    """The op the reference engine runs at engine/fused.py:295 on this GPU — torch's
+    F.scaled_dot_product_attention(q, k, v, attn_mask=bias) in bf16 with q (B, H, L, hd), k/v (B, H, K, hd)
+    holding the conditioning keys copied into every CFG row (engine/fused.py:127-136) and an additive bf16
+    bias (B, 1, 1, K), torch's own backend choice — beside sk_dit_attention on the same values, per c1 L x
+    {B3, B1} and c2 B3/B1. Both are graph-replayed over a pool of distinct input sets larger than L2.
+    Also times torch's cuDNN and memory-efficient backends forced one at a time (the flash backend takes
+    no additive mask). Reports microseconds per call, the ratio sdpa / ours, and the rel. L2 between them."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    import torch.nn.functional as F
+
+    from sokutou_b200 import dit, ops, workloads as W
+    out = {}
+    shapes = [(f"c1_L{L}", W.c1(L)) for L in W.C1_SWEEP] + [("c2", W.C2)]
+    for name, sh in shapes:
+        for B in (3, 1):
+            H, hd, L, S = sh.H, sh.hd, sh.L, sh.S
+            K = L + S
+            g = torch.Generator(device=device).manual_seed(11 + B)
+            per_set = 2 * (B * H * L * hd * 2 + 2 * B * H * K * hd) + 2 * S * H * hd * 2
+            sets = max(4, -(-min_pool_bytes // per_set))
+            bias4 = dit.cfg_bias(L, sh.Tb, sh.Sp, L, 40, device=device)[:B].contiguous()  # (B, K) bf16
+            pool = []
+            for _ in range(sets):
+                q = (torch.randn(B, H, L, hd, device=device, generator=g) * 0.5).bfloat16()
+                kl = (torch.randn(B, H, L, hd, device=device, generator=g) * 0.5).bfloat16()
+                vl = (torch.randn(B, H, L, hd, device=device, generator=g) * sh.sigma).bfloat16()
+                kc = (torch.randn(S, H, hd, device=device, generator=g) * 0.5).bfloat16()
+                vc = (torch.randn(S, H, hd, device=device, generator=g) * sh.sigma).bfloat16()
+                kf = torch.cat([kl, kc.permute(1, 0, 2).unsqueeze(0).expand(B, H, S, hd)], dim=2).contiguous()
+                vf = torch.cat([vl, vc.permute(1, 0, 2).unsqueeze(0).expand(B, H, S, hd)], dim=2).contiguous()
+                y_sk = torch.empty(B, L, H, hd, device=device, dtype=torch.bfloat16)
+                pool.append((q, kl, vl, kc, vc, kf, vf, y_sk))
+            mask = bias4.view(B, 1, 1, K)
+            res = {"B": B, "H": H, "hd": hd, "L": L, "K": K, "flops": sh.flops(B), "input_sets": sets}
+            try:
+                res["torch_backend"] = SDPBackend(int(torch._fused_sdp_choice(pool[0][0], pool[0][5], pool[0][6],
+                                                                              attn_mask=mask))).name
+            except Exception as e:  # a private helper: report what failed, the timing does not depend on it
+                res["torch_backend"] = f"unknown ({type(e).__name__})"
+
+            def run_sk():
+                for i in range(calls):
+                    q, kl, vl, kc, vc, kf, vf, y_sk = pool[i % sets]
+                    ops.dit_attention(q, kl, vl, kc, vc, bias4, out=y_sk)
+
+            def run_sdpa(backend=None):
+                def f():
+                    ctx = sdpa_kernel([backend]) if backend is not None else contextlib.nullcontext()
+                    with ctx:
+                        for i in range(calls):
+                            q, kl, vl, kc, vc, kf, vf, y_sk = pool[i % sets]
+                            F.scaled_dot_product_attention(q, kf, vf, attn_mask=mask)  # the engine's call, as is
+                return f
+
+            variants = [("sk", run_sk), ("sdpa", run_sdpa()), ("sdpa_cudnn", run_sdpa(SDPBackend.CUDNN_ATTENTION)),
+                        ("sdpa_efficient", run_sdpa(SDPBackend.EFFICIENT_ATTENTION))]
+            for key, fn in variants:
+                st = torch.cuda.Stream(device)
+                st.wait_stream(torch.cuda.current_stream(device))
+                try:
+                    with torch.cuda.stream(st):
+                        fn()
+                    torch.cuda.current_stream(device).wait_stream(st)
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr):
+                        fn()
+                except RuntimeError as e:  # a forced backend that refuses these inputs (same on every rank)
+                    torch.cuda.current_stream(device).wait_stream(st)
+                    torch.cuda.synchronize()
+                    res[f"{key}_us"] = None
+                    res[f"{key}_error"] = str(e).splitlines()[0][:160]
+                    continue
+                ms = time_graphs([gr], 3, 3, dist)
+                res[f"{key}_us"] = round(ms * 1e3 / (3 * calls), 3)
+                del gr
+            # the same call computed both ways (set 0): SDPA's (B, H, L, hd) against ours (B, L, H, hd)
+            q, kl, vl, kc, vc, kf, vf, y_sk = pool[0]
+            ops.dit_attention(q, kl, vl, kc, vc, bias4, out=y_sk)
+            y_t = F.scaled_dot_product_attention(q, kf, vf, attn_mask=mask).transpose(1, 2).float()
+            res["rel_l2_vs_sdpa"] = float((y_sk.float() - y_t).norm() / y_t.norm())
+            for key in ("sk", "sdpa", "sdpa_cudnn", "sdpa_efficient"):
+                if res.get(f"{key}_us"):
+                    res[f"{key}_tflops"] = round(sh.flops(B) / (res[f"{key}_us"] * 1e-6) / 1e12, 1)
+            if res.get("sk_us") and res.get("sdpa_us"):
+                res["speedup_vs_sdpa"] = round(res["sdpa_us"] / res["sk_us"], 3)
+            best = min((res[f"{k}_us"] for k in ("sdpa", "sdpa_cudnn", "sdpa_efficient") if res.get(f"{k}_us")),
+                       default=None)
+            if best and res.get("sk_us"):
+                res["speedup_vs_best_sdpa"] = round(best / res["sk_us"], 3)
+            out[f"{name}_b{B}"] = res
+            del pool
+            torch.cuda.empty_cache()
     return out
 
 
@@ -632,6 +796,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-serving", action="store_true")
     ap.add_argument("--only-c1", action="store_true", help="headline workload only (for launch-list captures)")
+    ap.add_argument("--skip", default="", help="comma list of extra sections to leave out: sdpa,layer,gemm,prefill,serving")
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU time budget of the reference arm")
     a = ap.parse_args()
     if a.impl == "reference":
@@ -710,13 +875,16 @@ def main():
     del dec
     torch.cuda.empty_cache()
 
-    # ---- fused attention block vs its three launches; Qwen3 prompt prefill
-    blocks = layer_block(dev, dist)
-    gemm = dit_gemm(dev, dist)
-    prefill = prefill_bench(dev, dist)
+    # ---- the reference's own op on this GPU (torch SDPA) beside ours; fused attention block vs its three
+    # launches; projection GEMMs beside cuBLAS; Qwen3 prompt prefill
+    skip = set(a.skip.split(",")) if a.skip else set()
+    sdpa = None if "sdpa" in skip else sdpa_gpu(dev, dist)
+    blocks = None if "layer" in skip else layer_block(dev, dist)
+    gemm = None if "gemm" in skip else dit_gemm(dev, dist)
+    prefill = None if "prefill" in skip else prefill_bench(dev, dist)
 
     # ---- c4 serving
-    serv = None if a.no_serving else serving(dist, dev)
+    serv = None if (a.no_serving or "serving" in skip) else serving(dist, dev)
     err = ops.device_error()
 
     # ---- CPU baseline (rank 0, N=1 only)
@@ -726,18 +894,13 @@ def main():
         cpu = {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
     if dist.rank == 0:
-        traffic = profile_traffic("dit_attn_tc_c1.md")
+        traffic = profile_traffic_mix("dit_attn_tc_c1.md", shapes)
         achieved = per_gpu  # every launch in the step is the DiT attention kernel: FLOPs/launch ÷ avg launch time
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": dist.world, "steps": a.steps,
             "warmup": max(a.warmup, 3), "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-            "config": {"workload": "BASELINE config 1: DiT attention, full synthesis (12 layers x 20 steps, "
-                                   "CFG B=3 on 10 steps, B=1 on 10) for L in 128/256/512",
-                       "heads": 12, "head_dim": 64, "text_keys": 64, "speaker_keys": 192,
-                       "calls_per_step": launches_step, "flops_per_step": flops_step,
-                       "parallelism": f"replicas x{dist.world}",
-                       "l2": "inputs larger than L2 (distinct q/k/v per call, ~3 GB per step)"},
+            "config": c1_config(dist.world, launches_step, flops_step),
             "per_L": per_L,
             "e2e": {"value": round(e2e_val, 4), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "path": "sokutou_b200.ops.dit_attention (C ABI) on pinned host buffers"},
@@ -745,7 +908,7 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": UNIT,
                          "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} bf16 burst",
                          "frac_of_spec": round(achieved / SPEC["bf16_tflops"], 4), "traffic": traffic},
-            "c2": c2_res, "c3": c3_res, "layer_block": blocks, "dit_gemm": gemm, "prefill": prefill, "serving": serv, "cpu_baseline": cpu,
+            "c2": c2_res, "c3": c3_res, "sdpa_gpu": sdpa, "layer_block": blocks, "dit_gemm": gemm, "prefill": prefill, "serving": serv, "cpu_baseline": cpu,
             "clocks": clk.summary(), "device_error": err,
         }
         print(json.dumps(line), flush=True)
@@ -772,8 +935,8 @@ def reference_arm(a):
     line = {"metric": METRIC, "value": round(v, 5), "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(el * 1e3 / max(a.steps, 1), 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "impl": "reference",
-            "config": {"workload": "BASELINE config 1: DiT attention, full synthesis for L in 128/256/512 "
-                                   "(CPU sample of the call mix)", "parallelism": "host CPU"},
+            "config": c1_config(world, sum(len(sh.synthesis_calls()) for sh in shapes),
+                                sum(sh.synthesis_flops() for sh in shapes)),
             "cpu_baseline": {"value": round(v, 5), "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": sample + "; torch F.scaled_dot_product_attention float32 with the ctx keys "
                                                 "copied per batch row, as the reference engine runs it"},

@@ -268,10 +268,12 @@ SK_API int sk_prefill_attention(const float* qkv, const float* qn, const float* 
  *
  * Same arguments and results as sk_decode_attention. The split-KV scratch is a 1 MiB array inside
  * the library's device image, one per device that loads the library, kept until the process exits.
- *   - Limit: the partials must fit 1 MiB minus 4 KiB, i.e. about nkv * ceil(max_len / 64) * 1040 bytes
- *     (nkv = 8: max_len up to 7936); larger calls return SK_ERR_TOO_LARGE and launch nothing.
- *   - The first call on each device looks up the array's address and zero-fills it, synchronously:
- *     make that first call before any stream capture.
+ *   - Limit: the partials, nkv * ceil(max_len / 64) * 1040 bytes, must fit 1 MiB minus 4 KiB
+ *     (1 044 480 bytes; nkv = 8: max_len up to 8000); larger calls return SK_ERR_TOO_LARGE and
+ *     launch nothing.
+ *   - The first call on each device looks up the array's address, zero-fills it and waits for the
+ *     whole device (cudaDeviceSynchronize) before it launches anything, so that first call may go on
+ *     any stream but must come before any stream capture.
  *   - Every call shares the array. Calls that may run at the same time on the GPU (different streams,
  *     or graphs replayed concurrently) race on it; serialise them or use sk_decode_attention.
  */

@@ -886,8 +886,11 @@ std::mutex g_static_mu;
 void* g_static_scratch_ptr[64] = {};
 
 // Device address of g_static_scratch on the current device. The first call on a device looks the
-// address up and zero-fills the array (synchronously), so that first call must come before any
-// stream capture.
+// address up and zero-fills the array, then waits for the whole device: cudaMemset returns before
+// the fill has finished and runs on the legacy default stream, which does not order against
+// non-blocking streams, so without the wait a first call on such a stream could start its kernel
+// on a half-cleared array. The pointer is published only after the fill is complete. Because of
+// that wait the first call must come before any stream capture.
 int static_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SK_ERR_CUDA;
@@ -896,6 +899,7 @@ int static_scratch(void** out) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, sk::decode::g_static_scratch) != cudaSuccess || !p) return SK_ERR_CUDA;
     if (cudaMemset(p, 0, sk::decode::kStaticScratchBytes) != cudaSuccess) return SK_ERR_CUDA;
+    if (cudaDeviceSynchronize() != cudaSuccess) return SK_ERR_CUDA;
     g_static_scratch_ptr[dev] = p;
   }
   *out = g_static_scratch_ptr[dev];

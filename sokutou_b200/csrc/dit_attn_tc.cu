@@ -129,30 +129,6 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-// 2^x for a pair, on the FMA/ALU pipes instead of the MUFU pipe: round-to-nearest range reduction
-// x = i + f, f in [-0.5, 0.5] (adding 1.5·2^23 leaves i in the low mantissa bits), 2^f by a degree-3
-// polynomial with p(0) = 1 fitted for this kernel by iteratively reweighted least squares on
-// Chebyshev points (max relative error 1.0e-4 in float32, far below the bf16 rounding of P), and i
-// added to the exponent field. Inputs are clamped at -127, which yields exactly 0 (masked keys).
-__device__ __forceinline__ float2 ex2_poly2(float2 x) {
-  x.x = fmaxf(x.x, -127.f);
-  x.y = fmaxf(x.y, -127.f);
-  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
-  const float2 r = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
-  const float2 f = __ffma2_rn(r, make_float2(-1.f, -1.f), x);
-  float2 q = __ffma2_rn(make_float2(0.05500892922282219f, 0.05500892922282219f), f,
-                        make_float2(0.2422109842300415f, 0.2422109842300415f));
-  q = __ffma2_rn(q, f, make_float2(0.6932829022407532f, 0.6932829022407532f));
-  q = __ffma2_rn(q, f, make_float2(1.f, 1.f));
-  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
-                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
-}
-// Exponent pairs per 8-key unit computed by ex2_poly2 instead of ex2.approx (MUFU), 0..4.
-// Measured on B200: 0 is fastest at these tile sizes (the softmax is not MUFU-bound).
-#ifndef SK_POLY_PAIRS
-#define SK_POLY_PAIRS 0
-#endif
-constexpr int kPolyPairs = SK_POLY_PAIRS;
 
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
   asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
@@ -593,9 +569,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 dd = __fadd2_rn(make_float2(x[c + 2 * e], x[c + 2 * e + 1]), nm);
-          const float2 p = (e < kPolyPairs) ? ex2_poly2(dd) : make_float2(ex2_approx(dd.x), ex2_approx(dd.y));
-          x[c + 2 * e] = p.x;
-          x[c + 2 * e + 1] = p.y;
+          x[c + 2 * e] = ex2_approx(dd.x);
+          x[c + 2 * e + 1] = ex2_approx(dd.y);
         }
       }
       // pass 2: row sum (two chains), bf16 packing, 16-byte swizzled stores of the P row
@@ -809,7 +784,7 @@ static int launch_tc(const void* q, const void* k_lat, const void* v_lat, const 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // set-up overlaps the previous kernel
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = sk::kUsePdl ? 1 : 0;
+  cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mkc, mvc, my, mg, prm) != cudaSuccess)
     return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;

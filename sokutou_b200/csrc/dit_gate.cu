@@ -115,7 +115,7 @@ extern "C" int sk_dit_gate(const void* y, const void* o4, void* out, long long r
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = sk::kUsePdl ? 1 : 0;
+  cfg.numAttrs = 1;
   cudaError_t e;
   if (dtype == SK_BF16) {
     const auto* yy = reinterpret_cast<const __nv_bfloat16*>(y);

@@ -223,7 +223,7 @@ static int launch(const void* x, const void* w, void* y, int M, int N, int K, co
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = sk::kUsePdl ? 1 : 0;
+  cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, linear_kernel<BN, FP8>, mx, mw, my, N, K, inv_x, inv_w, err) != cudaSuccess)
     return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;

@@ -160,7 +160,7 @@ int sk_launch_qkv_prologue(const void* o4, const float* qk_w, const float* freqs
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = sk::kUsePdl ? 1 : 0;
+  cfg.numAttrs = 1;
   const float inv = 1.f / hd;
   cudaError_t e = cudaSuccess;
 #define SK_PROLOGUE(T, HDV)                                                                                        \

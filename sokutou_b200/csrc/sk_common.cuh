@@ -45,12 +45,6 @@ __device__ __forceinline__ bool sk_in_bounds(bool cond, int* err) {
   return true;
 }
 #define SK_INB(cond, err) (!SK_BOUNDS_CHECK || sk_in_bounds((cond), (err)))
-// Programmatic dependent launch for the DiT kernels (each waits for its predecessor with
-// griddepcontrol.wait before reading global memory, so this only moves set-up earlier).
-#ifndef SK_USE_PDL
-#define SK_USE_PDL 1
-#endif
-constexpr bool kUsePdl = SK_USE_PDL != 0;
 
 // ---- mbarrier -------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -176,18 +176,38 @@ class GpuExecutor:
         self.dit = {}       # L -> (graph, buffers)
         self.dec = None     # (graph, TalkerAttention, buffers)
 
+    # Distinct q/k/v per attention call, as in the engine (each layer and step reads new projections):
+    # a pool of flat buffers larger than L2, rotated over the calls of every request, so no request
+    # replays from a warm L2. One pool serves every latent length (a call views a prefix).
+    POOL_BYTES = 384 << 20
+
+    def _pool(self):
+        import torch
+
+        from . import ops, workloads as W
+        if getattr(self, "_dit_pool", None) is None:
+            sh = W.c4_dit(W.C4_L_MAX)
+            per = 3 * sh.H * sh.L * sh.hd  # elements of one (B = 3, L max) q, k or v
+            n = max(8, -(-self.POOL_BYTES // (3 * per * 2)))
+            g = torch.Generator(device=self.device).manual_seed(17)
+            qk_w = W.dit_qk_weights(sh, self.device)
+            freqs = W.dit_freqs(sh.L, sh.hd, device=self.device)
+            sets = []
+            for _ in range(n):
+                o4 = (torch.randn(3 * sh.L, 4 * sh.H * sh.hd, device=self.device, generator=g) * sh.sigma).bfloat16()
+                q, k, v = ops.dit_qkv_prologue(o4, qk_w, freqs, 3, sh.L, sh.H, sh.hd, 1e-6)
+                sets.append((q.view(-1), k.view(-1), v.view(-1)))
+            self._dit_pool = sets
+            self._dit_y = torch.empty(per, device=self.device, dtype=torch.bfloat16)
+        return self._dit_pool, self._dit_y
+
     def _dit_graph(self, L: int):
         import torch
 
         from . import dit, ops, workloads as W
         sh = W.c4_dit(L)
+        sets, yflat = self._pool()
         g = torch.Generator(device=self.device).manual_seed(L)
-        bufs = {}
-        for B in (3, 1):
-            o4 = (torch.randn(B * L, 4 * sh.H * sh.hd, device=self.device, generator=g) * sh.sigma).bfloat16()
-            q, k, v = ops.dit_qkv_prologue(o4, W.dit_qk_weights(sh, self.device), W.dit_freqs(L, sh.hd, device=self.device),
-                                           B, L, sh.H, sh.hd, 1e-6)
-            bufs[B] = (q, k, v, torch.empty((B, L, sh.H, sh.hd), device=self.device, dtype=torch.bfloat16))
         ctx = []
         for _ in range(sh.n_layers):
             kc = torch.randn(sh.S, sh.H, sh.hd, device=self.device, generator=g)
@@ -198,11 +218,12 @@ class GpuExecutor:
 
         def run():
             for i, B in enumerate(sh.synthesis_calls()):
-                q, k, v, y = bufs[B]
+                n = B * sh.H * L * sh.hd
+                q, k, v = (t[:n].view(B, sh.H, L, sh.hd) for t in sets[i % len(sets)])
                 kc, vc = ctx[i % sh.n_layers]
-                ops.dit_attention(q, k, v, kc, vc, bias[:B], out=y)
+                ops.dit_attention(q, k, v, kc, vc, bias[:B], out=yflat[:n].view(B, L, sh.H, sh.hd))
 
-        return self._capture(run), (bufs, ctx, bias)
+        return self._capture(run), (ctx, bias)
 
     def _decode_graph(self):
         import torch

@@ -69,6 +69,9 @@ C1_SWEEP = (128, 256, 512)
 C2 = DitShape("c2", H=16, hd=128, L=512, Tb=128, Sp=384, n_layers=24, sigma=1 / math.sqrt(128), text_hi=128)
 
 
+C4_L_MAX = 384  # the largest latent length of a c4 DiT request (L ~ U[96, 384])
+
+
 def c4_dit(L: int) -> DitShape:
     return DitShape(f"c4_L{L}", H=16, hd=128, L=L, Tb=128, Sp=384, n_layers=24, sigma=1 / math.sqrt(128), text_hi=128)
 
@@ -148,7 +151,7 @@ def serving_requests(seed: int = 0, n_dit: int = 32, n_decode: int = 32):
     """The c4 request list: [(kind, size)] with kind 'dit' (size = latent length L ~ U[96,384]) or
     'decode' (size = final KV length T ~ U[200,1500]), interleaved in a seeded order."""
     g = torch.Generator().manual_seed(seed)
-    dit = [("dit", int(x)) for x in torch.randint(96, 385, (n_dit,), generator=g)]
+    dit = [("dit", int(x)) for x in torch.randint(96, C4_L_MAX + 1, (n_dit,), generator=g)]
     dec = [("decode", int(x)) for x in torch.randint(200, 1501, (n_decode,), generator=g)]
     order = torch.randperm(n_dit + n_decode, generator=g).tolist()
     reqs = dit + dec
