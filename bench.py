@@ -320,73 +320,87 @@ def time_graphs(graphs, steps: int, warmup: int, dist: Dist, label: str = "timed
 
 
 def dit_e2e(syn: list, steps: int, warmup: int, dist: Dist, device, depth: int = 3):
-    """Every call through the public op (ops.dit_attention, C ABI) with pinned host inputs and outputs:
-    each call's q/k/v copied host->device and its y copied back, all inside the timed region. Three
-    streams pipeline the calls: the inputs of call i+1 go up (copy-in stream) and the output of call i-1
-    comes back (copy-out stream) while call i computes, through a ring of `depth` device buffer sets
-    guarded by events — H2D and D2H use separate copy engines and overlap the kernels."""
+    """Every call through the public op (ops.dit_attention, C ABI) with inputs and outputs in pinned host
+    memory: per flow step, one host->device copy of the q/k/v of all its layers' calls, the calls, and
+    one device->host copy of their outputs, all inside the timed region. Three streams pipeline the flow
+    steps through a ring of `depth` device slots guarded by events: the inputs of step t+1 go up
+    (copy-in stream) and the outputs of step t-1 come back (copy-out stream) while step t computes —
+    H2D and D2H use separate copy engines and overlap the kernels."""
     from sokutou_b200 import ops
-    hosts = []
-    for s in syn:
-        # one call's inputs (the CFG batch of 3) in pinned host memory; every call re-sends its slice
-        hq, hk, hv = (t[0].cpu().pin_memory() for t in (s.q, s.k, s.v))
-        hy = torch.empty(s.y[0].shape, dtype=torch.bfloat16).pin_memory()
-        hctx = [(k.cpu().pin_memory(), v.cpu().pin_memory()) for k, v in s.ctx]
-        hb = s.bias.cpu().pin_memory()
-        ring = [tuple(torch.empty_like(t[0]) for t in (s.q, s.k, s.v, s.y)) for _ in range(depth)]
-        dctx = [(torch.empty_like(k), torch.empty_like(v)) for k, v in s.ctx]
-        hosts.append((hq, hk, hv, hy, hctx, hb, ring, dctx, torch.empty_like(s.bias)))
     s_in, s_cmp, s_out = (torch.cuda.Stream(device) for _ in range(3))
-    ev = lambda: torch.cuda.Event()
+    plans = []
+    for s in syn:
+        sh, nl = s.shape, s.shape.n_layers
+        per = {B: B * sh.H * sh.L * sh.hd for B in (1, 3)}  # elements of one call's q (or k, or v, or y)
+        host_in, host_out = {}, {}
+        for B in (1, 3):
+            # [layer][q | k | v] of one flow step's calls, from the first flow step with this batch size
+            first = s.calls.index(B)
+            blk = torch.empty(nl, 3, per[B], dtype=torch.bfloat16).pin_memory()
+            for li in range(nl):
+                for r, t in enumerate((s.q, s.k, s.v)):
+                    blk[li, r].copy_(t[first + li].reshape(-1))
+            host_in[B] = blk
+            host_out[B] = torch.empty(nl, per[B], dtype=torch.bfloat16).pin_memory()
+        ring = [(torch.empty(nl * 3 * per[3], dtype=torch.bfloat16, device=device),
+                 torch.empty(nl * per[3], dtype=torch.bfloat16, device=device)) for _ in range(depth)]
+        hctx = [(k.cpu().pin_memory(), v.cpu().pin_memory()) for k, v in s.ctx]
+        dctx = [(torch.empty_like(k), torch.empty_like(v)) for k, v in s.ctx]
+        hb = s.bias.cpu().pin_memory()
+        plans.append((s, per, host_in, host_out, ring, hctx, dctx, hb, torch.empty_like(s.bias)))
     h2d = d2h = 0
 
     def one_step(count):
         nonlocal h2d, d2h
-        for s, (hq, hk, hv, hy, hctx, hb, ring, dctx, dbias) in zip(syn, hosts):
-            nl = s.shape.n_layers
+        for s, per, host_in, host_out, ring, hctx, dctx, hb, dbias in plans:
+            sh, nl = s.shape, s.shape.n_layers
             with torch.cuda.stream(s_in):  # the synthesis' conditioning keys and mask, once
-                s_in.wait_stream(s_cmp)
                 dbias.copy_(hb, non_blocking=True)
                 for (dk, dv), (k, v) in zip(dctx, hctx):
                     dk.copy_(k, non_blocking=True)
                     dv.copy_(v, non_blocking=True)
             if count:
                 h2d += hb.numel() * 2 + sum(k.numel() * 2 + v.numel() * 2 for k, v in hctx)
-            free_in = [None] * depth   # the kernel that last read slot r's q/k/v
-            free_out = [None] * depth  # the copy that last read slot r's y
-            for i, B in enumerate(s.calls):
-                r = i % depth
-                q, k, v, y = (t[:B] for t in ring[r])
+            free_in = [None] * depth   # the kernels that last read slot r's inputs
+            free_out = [None] * depth  # the copy that last read slot r's outputs
+            n_steps = len(s.calls) // nl
+            for t in range(n_steps):
+                B = s.calls[t * nl]
+                r = t % depth
+                din, dout = ring[r]
+                n_in, n_out = nl * 3 * per[B], nl * per[B]
                 with torch.cuda.stream(s_in):
                     if free_in[r] is not None:
                         s_in.wait_event(free_in[r])
-                    q.copy_(hq[:B], non_blocking=True)
-                    k.copy_(hk[:B], non_blocking=True)
-                    v.copy_(hv[:B], non_blocking=True)
-                    landed = ev()
+                    din[:n_in].copy_(host_in[B].view(-1), non_blocking=True)
+                    landed = torch.cuda.Event()
                     landed.record(s_in)
                 with torch.cuda.stream(s_cmp):
                     s_cmp.wait_event(landed)
                     if free_out[r] is not None:
                         s_cmp.wait_event(free_out[r])
-                    kc, vc = dctx[i % nl]
-                    ops.dit_attention(q, k, v, kc, vc, dbias[:B], out=y)
-                    done = ev()
+                    x = din[:n_in].view(nl, 3, B, sh.H, sh.L, sh.hd)
+                    y = dout[:n_out].view(nl, B, sh.L, sh.H, sh.hd)
+                    for li in range(nl):
+                        kc, vc = dctx[li]
+                        ops.dit_attention(x[li, 0], x[li, 1], x[li, 2], kc, vc, dbias[:B], out=y[li])
+                    done = torch.cuda.Event()
                     done.record(s_cmp)
                     free_in[r] = done
                 with torch.cuda.stream(s_out):
                     s_out.wait_event(done)
-                    hy[:B].copy_(y, non_blocking=True)
-                    back = ev()
+                    host_out[B].view(-1).copy_(dout[:n_out], non_blocking=True)
+                    back = torch.cuda.Event()
                     back.record(s_out)
                     free_out[r] = back
                 if count:
-                    h2d += 3 * q.numel() * 2
-                    d2h += y.numel() * 2
-            for st in (s_in, s_cmp, s_out):  # the next synthesis reuses the ring and the ctx buffers
-                torch.cuda.current_stream(device).wait_stream(st)
+                    h2d += n_in * 2
+                    d2h += n_out * 2
+            cur = torch.cuda.current_stream(device)  # the next synthesis reuses the ring and ctx buffers
             for st in (s_in, s_cmp, s_out):
-                st.wait_stream(torch.cuda.current_stream(device))
+                cur.wait_stream(st)
+            for st in (s_in, s_cmp, s_out):
+                st.wait_stream(cur)
 
     for _ in range(warmup):
         one_step(False)
@@ -903,7 +917,7 @@ def main():
             "config": c1_config(dist.world, launches_step, flops_step),
             "per_L": per_L,
             "e2e": {"value": round(e2e_val, 4), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h), "path": "sokutou_b200.ops.dit_attention (C ABI) on pinned host buffers"},
+                    "d2h_bytes_per_step": int(d2h), "path": "sokutou_b200.ops.dit_attention (C ABI); per flow step one H2D of its calls' q/k/v from pinned host memory and one D2H of their outputs, pipelined over three streams"},
             "gpu_launches": launches_step * a.steps,
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": UNIT,
                          "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} bf16 burst",

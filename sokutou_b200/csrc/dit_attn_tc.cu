@@ -4,32 +4,41 @@
 // One CTA computes a 128-row query tile of one (batch, head) against all K = Lk + S keys, in key
 // tiles of 128:
 //
-//   warp 8 (one lane)  TMA producer: Q once, then K and V tiles into two rings of NSK and NSV slots,
-//                      released independently (a K slot as soon as S = Q·Kᵀ has consumed it, a V slot
-//                      when O += P·V has); the producer polls both rings. Latent keys come from
-//                      (B, H, Lk, hd), conditioning keys straight from their batch-shared (S, H, hd)
-//                      buffer — no per-CFG-branch copy.
-//   warp 9 (one lane)  MMA issuer: S_j = Q·K_jᵀ into TMEM buffer S[j % 2], O_w += P_j·V_j into the
-//                      TMEM accumulator O[j % 2], two tiles in flight.
+//   warp 8 (one lane)  TMA producer: Q once, then K_j and V_j for j = 0, 1, ... into two rings of NSK
+//                      and NSV slots, each copy waiting (asleep on the slot's mbarrier) for the MMA that
+//                      last read its slot. Latent keys come from (B, H, Lk, hd), conditioning keys
+//                      straight from their batch-shared (S, H, hd) buffer — no per-CFG-branch copy.
+//   warp 9 (one lane)  S issuer: S_j = Q·K_jᵀ into TMEM buffer S[j % 2], in order.
+//   warp 10 (one lane) P·V issuer: O_w += P_j·V_j into the TMEM accumulator O[j % 2] (w = j % 2), P read
+//                      from TMEM. Two issuing threads, because issuing a group of MMAs holds the thread
+//                      for about the group's run time in the tensor pipe: one thread for both streams
+//                      would keep a ready P·V waiting behind the next S.
+//   warp 11            (SKIP launches) the scan that lists the key tiles with a live key.
 //   warps 0-3, 4-7     two softmax warpgroups; warpgroup w takes the tiles j with j % 2 == w, so two
 //                      tiles' softmax run at once. Thread r of a warpgroup owns query row r (TMEM lane
 //                      r): it loads its S row (tcgen05.ld), applies scale and key bias (prefetched one
 //                      tile ahead) with packed fp32x2 FMAs, keeps a running max in the log2 domain,
-//                      writes P (bf16) as a 128B-swizzled shared-memory tile, and rescales its O row in
-//                      TMEM only when the max grew by more than 2^8 (exact either way: numerator and
-//                      denominator share the stale max).
+//                      exponentiates (3/4 on the MUFU unit, 1/4 by a cubic on the FMA pipe — the MUFU
+//                      unit's 16 results per clock bound the softmax otherwise), writes P (bf16 pairs)
+//                      back into tensor memory with tcgen05.st, and rescales its
+//                      O row in TMEM only when the max grew by more than 2^8 (exact either way:
+//                      numerator and denominator share the stale max).
 //   epilogue           the two (max, sum, O) partials of each row are merged, O / l -> bf16 ->
 //                      y (B, L, H, hd); warpgroup w writes half of the hd columns.
 // Every thread executes griddepcontrol.wait before touching global memory, so with programmatic
 // dependent launch a kernel's set-up (barriers, TMEM, descriptor prefetch) overlaps the tail of
 // the kernel before it while every input read still follows that kernel's completion.
 //
-// Operand layouts (all 128-byte swizzled, 1024-byte aligned, as TMA writes them):
+// Shared-memory operand layouts (128-byte swizzled, 1024-byte aligned, as TMA writes them):
 //   Q [128 rows][hd]   K-major A of S = Q·Kᵀ      (hd split in 64-element chunks)
 //   K [128 keys][hd]   K-major B of S
-//   P [128 rows][128]  K-major A of O = P·V        (keys split in 64-element chunks)
 //   V [128 keys][hd]   MN-major B of O (hd contiguous), LBO = chunk stride, SBO = 8 rows
-// TMEM: columns [0,128) S0, [128,256) S1, [256, 256+hd) O0, [256+hd, 256+2hd) O1; 512 allocated.
+// Tensor memory (512 columns, one lane per query row):
+//   hd = 64 :  S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384) P0 [384,448) P1 [448,512)
+//   hd = 128:  S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_w overlays the first 64 columns
+//              of S_w, so S_{j+2} is issued only once the P·V of tile j has completed.
+// P (the A operand of O += P·V): row r in lane r, keys 2c and 2c+1 as the low and high bf16 halves of
+// column c.
 #include <mutex>
 
 #include "sk_common.cuh"
@@ -39,7 +48,7 @@ namespace dit {
 
 constexpr int kBM = 128, kBN = 128;
 constexpr int kThreadsTC = 384;  // 2 softmax warpgroups + a warpgroup holding the producer and MMA warps
-constexpr int kWarpProducer = 8, kWarpMma = 9;
+constexpr int kWarpProducer = 8, kWarpMma = 9, kWarpPv = 10;  // TMA producer, S = Q·Kᵀ issuer, P·V issuer
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512); the producer/MMA
 // warpgroup gives registers back, the softmax warpgroups take them: 256 x 232 + 128 x 40 = 64512.
 constexpr int kLaunchRegs = 168, kSoftmaxRegs = 232, kControlRegs = 40;
@@ -47,17 +56,20 @@ static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreadsTC * kLaunchReg
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
 constexpr int kMaxLiveTiles = 64;     // key tiles per CTA up to which fully masked tiles are skipped
-constexpr int kWarpScan0 = 10;        // warps 10-11: the masked-tile scan (SKIP launches)
+constexpr int kWarpScan = 11;         // the masked-tile scan (SKIP launches)
+
 
 template <int HD>
 struct TcCfg;
 template <>
-struct TcCfg<64> {  // 16 + 4*16 + 4*16 + 2*32 = 208 KB
-  static constexpr int NSK = 4, NSV = 4;
+struct TcCfg<64> {  // 16 + 6*16 + 6*16 = 208 KB
+  static constexpr int NSK = 6, NSV = 6;
+  static constexpr int T_P = 384;  // P0 at 384, P1 at 448
 };
 template <>
-struct TcCfg<128> {  // 32 + 2*32 + 2*32 + 2*32 = 224 KB
-  static constexpr int NSK = 2, NSV = 2;
+struct TcCfg<128> {  // 32 + 3*32 + 3*32 = 224 KB
+  static constexpr int NSK = 3, NSV = 3;
+  static constexpr int T_P = 0;    // P_w overlays S_w
 };
 
 // Key tiles always run, masked or not: every latent tile and at least the first NSK (the producer and
@@ -75,14 +87,15 @@ struct TcLayout {
   static constexpr int NCH = HD / 64;              // 64-element (128-byte) chunks per row
   static constexpr int Q_BYTES = kBM * HD * 2;
   static constexpr int KV_BYTES = kBN * HD * 2;
-  static constexpr int P_BYTES = kBM * kBN * 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + NSK * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + NSV * KV_BYTES;       // one P tile per softmax warpgroup
+  // the y tile is staged over the K ring once every S = Q·Kᵀ has run (the epilogue waits for the last
+  // P·V, which the tensor pipe completes after every S)
+  static constexpr int OFF_Y = OFF_K;
   // float [2 wg][2 buf][kBN] key bias; after its tile loop a warpgroup reuses its own 2*kBN floats
   // for the (max, sum) of its kBM rows that the epilogue exchanges
-  static constexpr int OFF_BIAS = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_BIAS = OFF_V + NSV * KV_BYTES;
   static constexpr int OFF_BAR = OFF_BIAS + 4 * kBN * 4;
   // q_full, k_full/k_empty[NSK], v_full/v_empty[NSV], s_full[2], s_free[2], p_full[2], o_done[2], mma_done,
   // for the fused block: q_free, gate_full; live_ready (SKIP: the list of key tiles to run is built)
@@ -97,6 +110,10 @@ struct TcLayout {
   static constexpr int SMEM_ALLOC = BYTES;
   static_assert(SMEM_ALLOC <= 232448, "shared memory over the 227 KB per-CTA limit");
   static_assert(2 * kBM <= 2 * kBN, "the (max, sum) exchange must fit a warpgroup's bias area");
+  static_assert(NSK * KV_BYTES >= kBM * HD * 2, "the y tile must fit the K ring");
+  // tensor-memory columns (relative to the allocation)
+  static constexpr uint32_t T_S = 0, T_O = 256, T_P = TcCfg<HD>::T_P;
+  static constexpr bool P_OVER_S = (HD == 128);
 };
 
 struct TcParams {
@@ -130,6 +147,29 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 
+// 2^x for two values on the FMA pipe (for a share of the softmax exponentials, so that they do not all
+// queue on the 16-per-clock MUFU unit): x = n + f with n = round(x) (adding 1.5·2^23 rounds x into the
+// low mantissa bits), 2^f on [-0.5, 0.5] by the cubic 1 + f·(c1 + f·(c2 + f·c3)) whose coefficients
+// minimise the maximum relative error there (1.0e-4, found by reweighted least squares on Chebyshev
+// points; P is rounded to bf16 afterwards, 3.9e-3), and n added to the exponent field. x is clamped at
+// -127: then n = -127, f = 0 and the result is exactly +0, as ex2.approx gives for a masked key.
+__device__ __forceinline__ float2 exp2_fma_pair(float2 x) {
+  x.x = fmaxf(x.x, -127.f);
+  x.y = fmaxf(x.y, -127.f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 p = __ffma2_rn(make_float2(0.05500893f, 0.05500893f), f, make_float2(0.24221095f, 0.24221095f));
+  p = __ffma2_rn(p, f, make_float2(0.6932829f, 0.6932829f));
+  p = __ffma2_rn(p, f, make_float2(1.f, 1.f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+// Exponential pairs per 4 (of each 8 keys) computed by exp2_fma_pair: 1 of 4 (a quarter of them)
+// measured fastest on B200 — MUFU then carries 3/4 of the load, the FP32 pipe the rest; at half the
+// extra FMA-pipe instructions cost more than the MUFU time saved.
+constexpr int kFmaExpPairs = 1;
+
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
   asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
@@ -141,9 +181,11 @@ __device__ __forceinline__ void tma_store_commit_and_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
-// Key bias of column `col` of key tile j in the log2 domain; -inf past the end of its segment.
-__device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloat16* bias, int b, int j, int n_lat,
-                                           int col) {
+// Key bias of column `col` of key tile j as raw bf16 bits: 0xff80 (-inf) past the end of its segment,
+// 0 without a bias. Loaded a tile ahead and converted only where it is stored, so no arithmetic waits
+// for the load inside the tile that issues it.
+__device__ __forceinline__ uint32_t tile_bias_bits(const TcParams& prm, const __nv_bfloat16* bias, int b, int j,
+                                                   int n_lat, int col) {
   int key = -1;
   if (j < n_lat) {
     const int kk = j * kBN + col;
@@ -152,9 +194,16 @@ __device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloa
     const int kk = (j - n_lat) * kBN + col;
     key = kk < prm.S ? prm.Lk + kk : -1;
   }
-  if (key < 0) return -INFINITY;
-  if (!SK_INB(key < prm.Lk + prm.S && b < (int)gridDim.z, prm.err)) return 0.f;
-  return bias ? __bfloat162float(bias[(size_t)b * prm.bias_bs + key]) * kLog2e : 0.f;
+  if (key < 0) return 0xff80u;
+  if (!SK_INB(key < prm.Lk + prm.S && b < (int)gridDim.z, prm.err)) return 0u;
+  if (!bias) return 0u;
+  // issued here, where the program puts it: a plain load may be sunk by the scheduler towards its use
+  // a tile later, exposing the whole L2 round trip at the top of that tile
+  unsigned short v;
+  asm volatile("ld.global.nc.u16 %0, [%1];"
+               : "=h"(v)
+               : "l"(reinterpret_cast<const unsigned short*>(bias) + (size_t)b * prm.bias_bs + key));
+  return v;
 }
 
 // FUSED = false: attention over q (B, H, L, hd), latent k/v (B, H, Lk, hd) and the ctx K/V, y (B, L, H, hd).
@@ -168,7 +217,7 @@ __device__ __forceinline__ float tile_bias(const TcParams& prm, const __nv_bfloa
 // run. Warps 10-11 scan those tiles' bias at the start and publish the list of tiles to run through
 // live_ready; the producer, the MMA issuer and the softmax warpgroups work on the head tiles meanwhile
 // and read the list only when they get past them. Counts of tiles below are positions in that list;
-// tile_bias and the TMA coordinates take the key tile from it.
+// tile_bias_bits and the TMA coordinates take the key tile from it.
 template <int HD, bool FUSED, bool VO4, bool CAUSAL, bool SKIP>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -229,7 +278,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);  // one commit from each MMA-issuing thread
     if (FUSED) {
       mbar_init(q_free, 1);
       mbar_init(gate_full, 1);
@@ -262,7 +311,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   griddep_wait();
   griddep_launch_dependents();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 256;  // S[w] at tS + 128 w, O[w] at tO + HD w
+  // S[w] at tS + 128 w, O[w] at tO + HD w, P[w] at tP + 64 w (hd 64) or over S[w] (hd 128)
+  const uint32_t tS = tmem + Ly::T_S, tO = tmem + Ly::T_O, tP = tmem + Ly::T_P;
+  constexpr uint32_t kPStride = Ly::P_OVER_S ? 128 : 64;
   if (warp >= 8) {
   setmaxnreg_dec<kControlRegs>();
   if (warp == kWarpProducer) {
@@ -282,56 +333,51 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int c = 0; c < Ly::NCH; ++c) tma_prefetch_l2_3d(&tmG, 3 * prm.D + h * HD + c * 64, q0, b);
       }
+      // K_j then V_j for list entry j = 0, 1, ..., each waiting (asleep on its mbarrier) for its ring slot
+      // to be released by the MMA that last read it. SKIP: past the head tiles the list must be known.
       int jk = 0, jv = 0;
       bool ok = true;
-      // SKIP: list entries known to exist — the head tiles until the list is published
       bool known = !SKIP;
       int nt = SKIP ? kHead : ntiles;
-      const uint64_t t0 = globaltimer_ns();
-      uint32_t spins = 0;
-      while (ok && (!known || jk < nt || jv < nt)) {
-        bool progress = false;
-        if (SKIP && !known && mbar_test(live_ready, 0)) {
+      for (int j = 0; ok; ++j) {
+        if (SKIP && !known && j >= kHead) {
+          if (!(ok = mbar_wait(live_ready, 0, prm.err))) break;
           known = true;
           nt = *n_live_s;
         }
-        if (jk < nt && (jk < NSK || mbar_test(&k_empty[jk % NSK], ((jk / NSK) - 1) & 1))) {
-          const int s = jk % NSK;
-          const int tk = (SKIP && jk >= kHead) ? live_map[jk] : jk;  // key tile of list entry jk
+        if (j >= nt) break;
+        const int tj = (SKIP && j >= kHead) ? live_map[j] : j;  // key tile of list entry j
+        {
+          const int s = j % NSK;
+          if (j >= NSK && !(ok = mbar_wait(&k_empty[s], ((j / NSK) - 1) & 1, prm.err))) break;
           uint8_t* dst = smem + Ly::OFF_K + s * Ly::KV_BYTES;
           mbar_arrive_expect_tx(&k_full[s], Ly::KV_BYTES);
-          if (tk < n_lat) {
+          if (tj < n_lat) {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, tk * kBN, lzk);
+              tma_load_3d(dst + c * (kBN * 128), &tmK, &k_full[s], c * 64, tj * kBN, lzk);
           } else {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_4d(dst + c * (kBN * 128), &tmKc, &k_full[s], c * 64, h, (tk - n_lat) * kBN, bc);
+              tma_load_4d(dst + c * (kBN * 128), &tmKc, &k_full[s], c * 64, h, (tj - n_lat) * kBN, bc);
           }
-          ++jk;
-          progress = true;
+          jk = j + 1;
         }
-        if (jv < nt && jv < jk && (jv < NSV || mbar_test(&v_empty[jv % NSV], ((jv / NSV) - 1) & 1))) {
-          const int s = jv % NSV;
-          const int tv = (SKIP && jv >= kHead) ? live_map[jv] : jv;
+        {
+          const int s = j % NSV;
+          if (j >= NSV && !(ok = mbar_wait(&v_empty[s], ((j / NSV) - 1) & 1, prm.err))) break;
           uint8_t* dst = smem + Ly::OFF_V + s * Ly::KV_BYTES;
           mbar_arrive_expect_tx(&v_full[s], Ly::KV_BYTES);
-          if (tv < n_lat) {
+          if (tj < n_lat) {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_3d(dst + c * (kBN * 128), &tmV, &v_full[s], xv + c * 64, tv * kBN, lzv);
+              tma_load_3d(dst + c * (kBN * 128), &tmV, &v_full[s], xv + c * 64, tj * kBN, lzv);
           } else {
 #pragma unroll
             for (int c = 0; c < Ly::NCH; ++c)
-              tma_load_4d(dst + c * (kBN * 128), &tmVc, &v_full[s], c * 64, h, (tv - n_lat) * kBN, bc);
+              tma_load_4d(dst + c * (kBN * 128), &tmVc, &v_full[s], c * 64, h, (tj - n_lat) * kBN, bc);
           }
-          ++jv;
-          progress = true;
-        }
-        if (!progress && (++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-          set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
-          ok = false;
+          jv = j + 1;
         }
       }
       // fused: the gate tile goes where Q was, once no MMA reads Q any more (a blocking wait: the
@@ -350,90 +396,83 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int j = (jk > NSK ? jk - NSK : 0); j < jk; ++j) mbar_wait(&k_full[j % NSK], (j / NSK) & 1, prm.err);
       for (int j = (jv > NSV ? jv - NSV : 0); j < jv; ++j) mbar_wait(&v_full[j % NSV], (j / NSV) & 1, prm.err);
     }
-  } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------------ MMA issuer
+  } else if (warp == kWarpMma || warp == kWarpPv) {
+    // ------------------------------------------------------------------ MMA issuers
+    // Two threads issue tcgen05.mma: warp 9 every S = Q·Kᵀ, warp 10 every O += P·V. The issue of a group
+    // of MMAs (and its commit) holds the issuing thread for about the group's run time in the tensor
+    // pipe, so one thread doing both would hold a ready P·V behind the next S, and the reverse. Each
+    // thread commits its own completion barriers; the tensor pipe interleaves the two streams.
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idO = idesc_bf16_f32(kBM, HD, 0, 1);
-      const uint32_t aQ = sbase + Ly::OFF_Q, aK = sbase + Ly::OFF_K, aV = sbase + Ly::OFF_V, aP = sbase + Ly::OFF_P;
-      bool ok = mbar_wait(q_full, 0, prm.err);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % NSK, sb = j & 1;
-        if (!mbar_wait(&k_full[s], (j / NSK) & 1, prm.err)) return false;
-        if (j >= 2 && !mbar_wait(&s_free[sb], ((j - 2) >> 1) & 1, prm.err)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          const uint32_t offk = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-          tc_mma_ss(tS + sb * 128, smem_desc_sw128(aQ + off, 16, 1024),
-                    smem_desc_sw128(aK + s * Ly::KV_BYTES + offk, 16, 1024), idS, kk > 0);
-        }
-        tc_commit(&s_full[sb]);
-        tc_commit(&k_empty[s]);  // the K slot is free once this S is computed
-        return true;
-      };
-      // S_j needs K_j and its S buffer read (the softmax of tile j-2 has loaded it); PV_j needs P_j
-      // and V_j. Both are issued as soon as their inputs are ready, S first: a softmax warpgroup
-      // never waits for the P·V of its previous tile before its next S is there.
-      auto issue_pv = [&](int j) {
-        const int sv = j % NSV, w = j & 1;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t offp = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          tc_mma_ss(tO + w * HD, smem_desc_sw128(aP + w * Ly::P_BYTES + offp, 16, 1024),
-                    smem_desc_sw128(aV + sv * Ly::KV_BYTES + kk * 2048, kBN * 128, 1024), idO, (j >= 2 || kk > 0));
-        }
-        tc_commit(&o_done[w]);
-        tc_commit(&v_empty[sv]);
-      };
-      int js = 0, jp = 0;
+      const uint32_t aQ = sbase + Ly::OFF_Q, aK = sbase + Ly::OFF_K, aV = sbase + Ly::OFF_V;
+      bool ok = true;
       // SKIP: list entries known to exist — the head tiles until the list is published
       bool known = !SKIP;
       int nt = SKIP ? kHead : ntiles;
-      const uint64_t t0 = globaltimer_ns();
-      uint32_t spins = 0;
-      while (ok && (!known || jp < nt)) {
-        bool progress = false;
-        if (SKIP && !known && mbar_test(live_ready, 0)) {
+      auto know = [&](int j) -> bool {  // is it settled whether list entry j exists?
+        if (SKIP && !known && j >= kHead) {
+          if (!mbar_wait(live_ready, 0, prm.err)) return false;
           known = true;
           nt = *n_live_s;
-          if (FUSED && js == nt) tc_commit(q_free);  // the head tiles were all there is
         }
-        if (js < nt && js < jp + 4 && mbar_test(&k_full[js % NSK], (js / NSK) & 1) &&
-            (js < 2 || mbar_test(&s_free[js & 1], ((js - 2) >> 1) & 1))) {
-          ok = issue_s(js);  // its waits are already satisfied
-          ++js;
-          if (FUSED && known && js == nt) tc_commit(q_free);  // Q is read by no further MMA
-          progress = true;
+        return true;
+      };
+      if (warp == kWarpMma) {
+        // S_j = Q·K_jᵀ into S[j % 2]: K_j landed, S[j % 2] loaded by the softmax of entry j-2 and, where P
+        // overlays S, the P·V of entry j-2 complete. Frees the K slot.
+        ok = mbar_wait(q_full, 0, prm.err);
+        for (int j = 0; ok; ++j) {
+          if (!(ok = know(j))) break;
+          if (j >= nt) break;
+          const int w = j & 1, slot = j % NSK;
+          if (!(ok = mbar_wait(&k_full[slot], (j / NSK) & 1, prm.err))) break;
+          if (j >= 2 && !(ok = mbar_wait(&s_free[w], ((j - 2) >> 1) & 1, prm.err))) break;
+          if (Ly::P_OVER_S && j >= 2 && !(ok = mbar_wait(&o_done[w], ((j - 2) >> 1) & 1, prm.err))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+            tc_mma_ss(tS + w * 128, smem_desc_sw128(aQ + off, 16, 1024),
+                      smem_desc_sw128(aK + slot * Ly::KV_BYTES + off, 16, 1024), idS, kk > 0);
+          }
+          tc_commit(&s_full[w]);
+          tc_commit(&k_empty[slot]);
         }
-        if (ok && jp < js && mbar_test(&p_full[jp & 1], (jp >> 1) & 1) &&
-            mbar_test(&v_full[jp % NSV], (jp / NSV) & 1)) {
-          issue_pv(jp);
-          ++jp;
-          progress = true;
-        }
-        if (!progress && (++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-          set_dev_error(prm.err, SK_DEVERR_TIMEOUT);
-          ok = false;
+        if (FUSED) tc_commit(q_free);  // every S issued: Q is read by no further MMA once they complete
+      } else {
+        // O_w += P_j·V_j (w = j % 2), P read from tensor memory: P_j written and V_j landed. Frees the V slot.
+        for (int j = 0; ok; ++j) {
+          if (!(ok = know(j))) break;
+          if (j >= nt) break;
+          const int w = j & 1, sv = j % NSV;
+          if (!(ok = mbar_wait(&p_full[w], (j >> 1) & 1, prm.err))) break;
+          if (!(ok = mbar_wait(&v_full[sv], (j / NSV) & 1, prm.err))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            tc_mma_ts(tO + w * HD, tP + w * kPStride + kk * 8,
+                      smem_desc_sw128(aV + sv * Ly::KV_BYTES + kk * 2048, kBN * 128, 1024), idO, (j >= 2 || kk > 0));
+          tc_commit(&o_done[w]);
+          tc_commit(&v_empty[sv]);
         }
       }
+      // both threads: every MMA this CTA issued has completed before TMEM is released
       tc_commit(mma_done);
       mbar_wait(mma_done, 0, prm.err);
     }
-  } else if (SKIP && warp >= kWarpScan0) {
-    // ------------------------------------------------------------------ masked-tile scan (warps 10-11)
-    // warp w takes tiles kHead + w, + 2, ... two at a time, lane l testing keys l, l + 32, l + 64, l + 96
-    // of each: 16-bit loads compared with the bits of a bf16 -inf (0xff80), so a tile runs if any key's
-    // bias is anything else (NaN included, as in the softmax). Integer work on few registers, so that
-    // all eight loads of a lane are in flight together.
+  } else if (SKIP && warp == kWarpScan) {
+    // ------------------------------------------------------------------ masked-tile scan (warp 11)
+    // tiles kHead, kHead + 1, ... two at a time, lane l testing keys l, l + 32, l + 64, l + 96 of each:
+    // 16-bit loads compared with the bits of a bf16 -inf (0xff80), so a tile runs if any key's bias is
+    // anything else (NaN included, as in the softmax). Integer work on few registers, so that all eight
+    // loads of a lane are in flight together.
     const unsigned short* brow = reinterpret_cast<const unsigned short*>(prm.bias) + (size_t)b * prm.bias_bs;
-    for (int j0 = kHead + (warp - kWarpScan0); j0 < ntiles; j0 += 4) {
+    for (int j0 = kHead; j0 < ntiles; j0 += 2) {
       unsigned short bits[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const int j = j0 + 2 * (e >> 2), col = lane + 32 * (e & 3);
+        const int j = j0 + (e >> 2), col = lane + 32 * (e & 3);
         // key of column col of tile j: latent keys [0, Lk), then the conditioning keys [Lk, Lk + S)
         const int kk = j < n_lat ? j * kBN + col : (j - n_lat) * kBN + col;
         const bool in = j < ntiles && (j < n_lat ? kk < prm.Lk : kk < prm.S);
@@ -444,11 +483,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int u = 0; u < 2; ++u) {
         const bool any = (bits[4 * u] != 0xff80u) | (bits[4 * u + 1] != 0xff80u) | (bits[4 * u + 2] != 0xff80u) |
                          (bits[4 * u + 3] != 0xff80u);
-        if (__any_sync(0xffffffffu, any) && lane == 0) atomicOr(live_mask, 1ull << (j0 + 2 * u));
+        if (__any_sync(0xffffffffu, any) && lane == 0) atomicOr(live_mask, 1ull << (j0 + u));
       }
     }
-    named_bar_sync(4, 64);
-    if (warp == kWarpScan0) {  // the list: tiles with their bit set (the head tiles among them), in order
+    __syncwarp();
+    {  // the list: tiles with their bit set (the head tiles among them), in order
       const unsigned long long mk = *reinterpret_cast<volatile unsigned long long*>(live_mask);
       const unsigned lo = (unsigned)mk, hi = (unsigned)(mk >> 32);
       const unsigned below = (1u << lane) - 1u;
@@ -468,7 +507,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int row = threadIdx.x & 127;  // TMEM lane == query row within the tile
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(prm.bias);
-    uint8_t* prow = smem + Ly::OFF_P + wg * Ly::P_BYTES + row * 128;
     const float2 sl2 = make_float2(prm.scale_log2, prm.scale_log2);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -476,7 +514,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // entry wg is tile wg)
     int nt = SKIP ? kHead : ntiles;
     bool known = !SKIP;
-    float bnext = (wg < ntiles) ? tile_bias(prm, bias, b, wg, n_lat, row) : 0.f;
+    uint32_t bnext = (wg < ntiles) ? tile_bias_bits(prm, bias, b, wg, n_lat, row) : 0u;
     for (int i = wg; ok; i += 2) {
       if (SKIP && !known && i + 2 >= kHead) {  // the next prefetch may need the list
         known = true;
@@ -490,9 +528,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const int j = (SKIP && i >= kHead) ? live_map[i] : i;  // the key tile of list entry i
       const int it = i >> 1;  // this warpgroup's tile count so far
       float* bt = bias_s + (wg * 2 + (it & 1)) * kBN;
-      if (SK_INB(row < kBN && wg * 2 + (it & 1) < 4, prm.err)) bt[row] = bnext;
+      if (SK_INB(row < kBN && wg * 2 + (it & 1) < 4, prm.err)) bt[row] = bf16_bits_to_f32(bnext) * kLog2e;
       if (i + 2 < nt)  // lands during this tile
-        bnext = tile_bias(prm, bias, b, (SKIP && i + 2 >= kHead) ? live_map[i + 2] : i + 2, n_lat, row);
+        bnext = tile_bias_bits(prm, bias, b, (SKIP && i + 2 >= kHead) ? live_map[i + 2] : i + 2, n_lat, row);
       named_bar_sync(1 + wg, 128);
       if (!mbar_wait(&s_full[wg], it & 1, prm.err)) {
         ok = false;
@@ -563,24 +601,27 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       const float2 nm = make_float2(-m_use, -m_use);
-      // pass 1: all 128 exponentials in place (independent, so the MUFU pipe stays fed)
+      // pass 1: all 128 exponentials in place (independent, so the MUFU pipe stays fed; a quarter of them
+      // on the FMA pipe)
 #pragma unroll
       for (int c = 0; c < kBN; c += 8) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 dd = __fadd2_rn(make_float2(x[c + 2 * e], x[c + 2 * e + 1]), nm);
-          x[c + 2 * e] = ex2_approx(dd.x);
-          x[c + 2 * e + 1] = ex2_approx(dd.y);
+          const float2 pe = (e < kFmaExpPairs) ? exp2_fma_pair(dd) : make_float2(ex2_approx(dd.x), ex2_approx(dd.y));
+          x[c + 2 * e] = pe.x;
+          x[c + 2 * e + 1] = pe.y;
         }
       }
-      // pass 2: row sum (two chains), bf16 packing, 16-byte swizzled stores of the P row
+      // pass 2: row sum (two chains) and bf16 packing of the P row, 32 columns of it per tcgen05.st into
+      // this warpgroup's P columns (lane = row; keys 2c, 2c+1 the low and high halves of column c)
       float2 ls0 = make_float2(0.f, 0.f), ls1 = ls0;
 #pragma unroll
-      for (int u = 0; u < kBN / 8; ++u) {
-        uint32_t pk[4];
+      for (int h32 = 0; h32 < 2; ++h32) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 p = make_float2(x[8 * u + 2 * e], x[8 * u + 2 * e + 1]);
+        for (int e = 0; e < 32; ++e) {
+          const float2 p = make_float2(x[64 * h32 + 2 * e], x[64 * h32 + 2 * e + 1]);
           if (e & 1)
             ls1 = __fadd2_rn(ls1, p);
           else
@@ -588,14 +629,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const __nv_bfloat162 pb2 = __floats2bfloat162_rn(p.x, p.y);
           pk[e] = *reinterpret_cast<const uint32_t*>(&pb2);
         }
-        const int chunk = u >> 3, unit = u & 7;
-        const int poff = chunk * (kBM * 128) + row * 128 + ((unit ^ (row & 7)) << 4);  // within this group's P tile
-        if (SK_INB(poff + 16 <= Ly::P_BYTES, prm.err))
-          *reinterpret_cast<uint4*>(prow + chunk * (kBM * 128) + ((unit ^ (row & 7)) << 4)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tmem_st32(tP + wg * kPStride + lane_off + 32 * h32, reinterpret_cast<const float*>(pk));
       }
       l_run += (ls0.x + ls0.y) + (ls1.x + ls1.y);
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[wg]);
     }
@@ -626,8 +663,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const float l = a0 * l0 + a1 * l1;
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
       const float c0 = a0 * inv, c1 = a1 * inv;
-      // y tile staged as 128B-swizzled [128 rows][64 cols] chunks over the (now free) P tiles, then
-      // written by TMA tensor stores; rows past L are clipped by the tensor map.
+      // y tile staged as 128B-swizzled [128 rows][64 cols] chunks over the K ring (free: the last P·V
+      // completes after every S in the in-order tensor pipe), then written by TMA tensor stores; rows
+      // past L are clipped by the tensor map.
       constexpr int NC = HD / 64;  // 32-column pieces per warpgroup half
       float o0[NC][32], o1[NC][32];
 #pragma unroll
@@ -640,7 +678,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
         const int col = wg * (HD / 2) + c * 32;  // first column of this piece
-        uint8_t* chunk = smem + Ly::OFF_P + (col >> 6) * (kBM * 128) + row * 128;
+        uint8_t* chunk = smem + Ly::OFF_Y + (col >> 6) * (kBM * 128) + row * 128;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint32_t pk[4];
@@ -668,7 +706,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             const __nv_bfloat162 v2 = __floats2bfloat162_rn(y0, y1);
             pk[e] = *reinterpret_cast<const uint32_t*>(&v2);
           }
-          if (SK_INB((col >> 6) * (kBM * 128) + row * 128 + ((unit ^ (row & 7)) << 4) + 16 <= 2 * Ly::P_BYTES, prm.err))
+          if (SK_INB((col >> 6) * (kBM * 128) + row * 128 + ((unit ^ (row & 7)) << 4) + 16 <= Ly::NSK * Ly::KV_BYTES, prm.err))
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(chunk + ((unit ^ (row & 7)) << 4))),
                          "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3])
                          : "memory");
@@ -679,7 +717,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     named_bar_sync(3, 256);
     if (okk && threadIdx.x == 0) {
 #pragma unroll
-      for (int c = 0; c < Ly::NCH; ++c) tma_store_4d(&tmY, smem + Ly::OFF_P + c * (kBM * 128), c * 64, h, q0, b);
+      for (int c = 0; c < Ly::NCH; ++c) tma_store_4d(&tmY, smem + Ly::OFF_Y + c * (kBM * 128), c * 64, h, q0, b);
       tma_store_commit_and_wait_read();
     }
   }

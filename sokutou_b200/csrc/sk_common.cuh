@@ -84,14 +84,30 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may keep the thread suspended for up to kSuspendHintNs (woken as soon as the phase
+// completes): a waiting warp takes no issue slots from the warps sharing its sub-partition.
+constexpr uint32_t kSuspendHintNs = 100000;
+
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
 // Waits until the phase with the given parity has completed. Returns false (and records
 // SK_DEVERR_TIMEOUT in *err) if that takes longer than kWaitLimitNs; the caller then unwinds.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test(bar, parity)) return true;  // already complete: no suspend round trip
+  if (mbar_try_wait_sleep(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((i & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
       set_dev_error(err, SK_DEVERR_TIMEOUT);
       return false;
     }
@@ -227,6 +243,19 @@ __device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] · B[smem]ᵀ, kind::f16: A (M x 16) read from tensor memory — row m in lane m,
+// the 16 bf16 elements of the k step packed two per 32-bit column (element 2c in the low half of
+// column a_tmem + c) — so a product computed in registers goes to the tensor core without a trip
+// through shared memory. A must be K-major (instruction descriptor bit 15 = 0).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // The same with 8-bit operands, kind::f8f6f4 (K = 32 per instruction; formats from the descriptor).
