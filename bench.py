@@ -731,6 +731,79 @@ def dit_gemm(device, dist: Dist, calls: int = 60, sets: int = 4) -> dict:
     return out
 
 
+# ------------------------------------------------------------------------------- fused decode layer block
+def decode_block_bench(device, dist: Dist, hidden: int = 2048, lo: int = 1023, hi: int = 1120) -> dict:
+    """One talker layer's attention block — rms_gemv(qkv) -> attention -> gemv(o), the three launches of
+    qwen3/kernels.py:619-624 — at the 1.7B talker's width (hidden 2048, bf16 weights, bf16 cache), decoding
+    positions lo..hi-1 (T >= 1024) through all 28 layers with distinct weights per layer (0.7 GB, far past
+    L2), graph-replayed: the one-launch kernel (sk_decode_attention_block) against the same block as three
+    launches (torch's bf16 GEMVs around sk_decode_attention). Bytes per layer: both weight matrices, the
+    K/V read and append, qkv/att/h traffic."""
+    from sokutou_b200 import ops, qwen3, workloads as W
+    s = W.C3
+    nl, nq, nkv, hd = s.n_layers, s.nq, s.nkv, s.hd
+    g = torch.Generator(device=device).manual_seed(21)
+    Dq = (nq + 2 * nkv) * hd
+    wq = (torch.randn(nl, Dq, hidden, device=device, generator=g) / hidden ** 0.5).bfloat16()
+    wo = (torch.randn(nl, hidden, nq * hd, device=device, generator=g) / (nq * hd) ** 0.5).bfloat16()
+    nw = 1 + 0.1 * torch.randn(nl, hidden, device=device, generator=g)
+    qn = 1 + 0.02 * torch.randn(nl, hd, device=device, generator=g)
+    kn = 1 + 0.02 * torch.randn(nl, hd, device=device, generator=g)
+    ta = qwen3.TalkerAttention(nl, nq, nkv, 1536, s.theta, s.eps, device, torch.bfloat16)
+    ta.k.copy_(torch.randn(ta.k.shape, device=device, generator=g))
+    ta.v.copy_(torch.randn(ta.v.shape, device=device, generator=g))
+    h = torch.randn(hidden, device=device, generator=g)
+    qkv = torch.empty(Dq, device=device)
+    att = torch.empty(nq * hd, device=device)
+
+    def fused():
+        for li in range(nl):
+            ta.block(li, h, nw[li], s.eps, wq[li], qn[li], kn[li], wo[li], kv_stable=li > 0)
+        ta.pos.add_(1)
+
+    def separate():
+        for li in range(nl):
+            x = (h * nw[li] * torch.rsqrt((h * h).mean() + s.eps)).bfloat16()
+            qkv.copy_(torch.mv(wq[li], x))
+            ta.attn(li, qkv, qn[li], kn[li], att, kv_stable=li > 0)
+            h.add_(torch.mv(wo[li], att.bfloat16()))
+        ta.pos.add_(1)
+
+    res = {"hidden": hidden, "layers": nl, "weights": "bf16", "cache": "bf16", "T_range": [lo + 1, hi]}
+    w_bytes = (Dq + hidden) * hidden * 2
+    tot = sum(w_bytes + s.layer_bytes(p + 1) + 2 * hidden * 4 for p in range(lo, hi)) * nl
+    for name, fn in (("fused", fused), ("separate", separate)):
+        st = torch.cuda.Stream(device)
+        st.wait_stream(torch.cuda.current_stream(device))
+        ta.pos.fill_(lo)
+        with torch.cuda.stream(st):
+            fn()
+        torch.cuda.current_stream(device).wait_stream(st)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        ta.pos.fill_(lo)
+        gr.replay()  # warm-up
+        torch.cuda.synchronize()
+        dist.barrier()
+        ta.pos.fill_(lo)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(lo, hi):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = dist.max(e0.elapsed_time(e1))
+        del gr
+        res[f"{name}_us_per_layer"] = round(ms * 1e3 / ((hi - lo) * nl), 3)
+        res[f"{name}_gbs"] = round(tot / (ms / 1e3) / 1e9, 1)
+    res["bytes_per_layer_at_T1120"] = w_bytes + s.layer_bytes(hi) + 2 * hidden * 4
+    res["speedup"] = round(res["separate_us_per_layer"] / res["fused_us_per_layer"], 3)
+    del wq, wo, ta
+    torch.cuda.empty_cache()
+    return res
+
+
 # ------------------------------------------------------------------------------------------- prefill
 def prefill_bench(device, dist: Dist) -> dict:
     """The c3 prompt (and a 160-token one) through all 28 talker layers' prefill attention, graph-replayed,
@@ -810,7 +883,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-serving", action="store_true")
     ap.add_argument("--only-c1", action="store_true", help="headline workload only (for launch-list captures)")
-    ap.add_argument("--skip", default="", help="comma list of extra sections to leave out: sdpa,layer,gemm,prefill,serving")
+    ap.add_argument("--skip", default="", help="comma list of extra sections to leave out: sdpa,layer,gemm,prefill,block,serving")
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU time budget of the reference arm")
     a = ap.parse_args()
     if a.impl == "reference":
@@ -896,6 +969,9 @@ def main():
     blocks = None if "layer" in skip else layer_block(dev, dist)
     gemm = None if "gemm" in skip else dit_gemm(dev, dist)
     prefill = None if "prefill" in skip else prefill_bench(dev, dist)
+    dblock = None if "block" in skip else decode_block_bench(dev, dist)
+    if dblock:
+        dblock["fused_frac_of_measured_hbm"] = round(dblock["fused_gbs"] / pk["hbm_gbs"], 4)
 
     # ---- c4 serving
     serv = None if (a.no_serving or "serving" in skip) else serving(dist, dev)
@@ -922,7 +998,7 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": UNIT,
                          "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} bf16 burst",
                          "frac_of_spec": round(achieved / SPEC["bf16_tflops"], 4), "traffic": traffic},
-            "c2": c2_res, "c3": c3_res, "sdpa_gpu": sdpa, "layer_block": blocks, "dit_gemm": gemm, "prefill": prefill, "serving": serv, "cpu_baseline": cpu,
+            "c2": c2_res, "c3": c3_res, "sdpa_gpu": sdpa, "layer_block": blocks, "dit_gemm": gemm, "prefill": prefill, "decode_block": dblock, "serving": serv, "cpu_baseline": cpu,
             "clocks": clk.summary(), "device_error": err,
         }
         print(json.dumps(line), flush=True)

@@ -259,6 +259,36 @@ SK_API int sk_prefill_attention(const float* qkv, const float* qn, const float* 
                                 int nq, int nkv, int hd, void* out, void* q_buf, int cache_dtype,
                                 void* stream);
 
+/* Bytes of workspace sk_decode_attention_block needs for caches of max_len positions. */
+SK_API size_t sk_decode_block_workspace_bytes(int max_len, int nq, int nkv, int hd);
+
+/*
+ * One talker layer's whole attention block in a single launch — the three launches the reference
+ * makes per layer at qwen3/kernels.py:619-624:
+ *   rms_gemv(qkv) (qwen3/kernels.py:271-275):  qkv = W_qkv · (h ⊙ in_norm) · 1/sqrt(mean(h²) + eps_in)
+ *   attn          (qwen3/kernels.py:341-414):  att = the decode attention of sk_decode_attention on qkv
+ *                                              (QK-RMSNorm, RoPE, K/V appended at pos, GQA over T = pos + 1)
+ *   gemv(o)       (qwen3/kernels.py:301-305):  h += W_o · att   (accumulate = 1: the residual add)
+ *
+ *   h        : fp32 [hidden], the residual stream, updated in place
+ *   in_norm  : fp32 [hidden], the layer's input RMSNorm weight; eps_in its epsilon
+ *   w_qkv    : [(nq + 2*nkv) * hd][hidden] (q rows, then k, then v), bf16 or fp32 (weight_dtype)
+ *   w_o      : [hidden][nq * hd], same dtype
+ *   qn, kn, eps, rope, Kc, Vc, pos_ptr, pos_add, max_len, nq, nkv, hd, cache_dtype: as sk_decode_attention
+ *   workspace: caller-owned, sk_decode_block_workspace_bytes() bytes, zero-filled once before first use
+ *              (every launch leaves its counters at zero; after a device error, zero it again)
+ *   flags    : 0 or SK_DECODE_KV_STABLE (the position and this layer's cache rows may be read before the
+ *              kernel just before has finished; the weights are always prefetched before that wait)
+ * One cooperative launch (one CTA per SM, all resident) with two grid-wide barriers between the
+ * phases; no float atomics, so results are identical from run to run. hidden a multiple of 8; all
+ * pointers 16-byte aligned; hd = 128, nq = 2*nkv.
+ */
+SK_API int sk_decode_attention_block(float* h, const float* in_norm, float eps_in, const void* w_qkv,
+                                     const float* qn, const float* kn, float eps, const float* rope,
+                                     void* Kc, void* Vc, const long long* pos_ptr, int pos_add, int max_len,
+                                     int nq, int nkv, int hd, const void* w_o, int hidden, int weight_dtype,
+                                     int cache_dtype, void* workspace, size_t ws_bytes, int flags, void* stream);
+
 /*
  * sk_decode_attention without a workspace argument: allocates nothing, for callers that cannot call
  * cudaMalloc when they attend (a serving process that reserves its device memory up front and

@@ -113,6 +113,32 @@ def decode_step_f32(qkv, qn, kn, eps, rope, Kc, Vc, pos: int, nq: int, nkv: int,
     return out.reshape(-1)
 
 
+def rms_gemv(h, nw, eps: float, W):
+    """out = W · RMSNorm(h) with the RMSNorm weight nw — the reference's `rms_gemv` (qwen3/kernels.py:271-275:
+    gemv_core :152-255 + rms_gemv_body :257-270): x = h ⊙ nw, inv = 1/sqrt(Σh²/K + eps), out[r] =
+    (Σ_k W[r,k]·x[k])·inv. float64; W as stored (bf16 or fp32 values)."""
+    h = np.asarray(h, np.float64)
+    x = h * np.asarray(nw, np.float64)
+    inv = 1.0 / np.sqrt((h * h).mean() + eps)
+    return (np.asarray(W, np.float64) @ x) * inv
+
+
+def gemv_acc(x, W, out):
+    """out + W · x — the reference's `gemv` with accumulate = 1 (qwen3/kernels.py:301-305, gemv_body :285-300):
+    the o projection added into the residual stream. float64."""
+    return np.asarray(out, np.float64) + np.asarray(W, np.float64) @ np.asarray(x, np.float64)
+
+
+def decode_block(h, in_norm, eps_in: float, w_qkv, qn, kn, eps: float, rope, Kc, Vc, pos: int, nq: int, nkv: int,
+                 w_o, cache_dtype: str = "bf16"):
+    """One talker layer's attention block as the reference launches it at qwen3/kernels.py:619-624:
+    rms_gemv(qkv) -> attn -> gemv(o) accumulating into the residual h. Mutates Kc/Vc at `pos` (the
+    attention appends k/v); returns the new h (float64)."""
+    qkv = rms_gemv(h, in_norm, eps_in, w_qkv)
+    att = decode_step(qkv, qn, kn, eps, rope, Kc, Vc, pos, nq, nkv, cache_dtype)
+    return gemv_acc(att, w_o, h)
+
+
 def talker_greedy(weights: dict, n_layers: int, nq: int, nkv: int, hd: int, max_len: int, prompt_len: int,
                   n_new: int, eps: float, rope, cache_dtype: str = "f32"):
     """Greedy tokens of the synthetic talker stack, float64 (see sokutou_b200.workloads.SyntheticTalker).

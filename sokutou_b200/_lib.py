@@ -39,6 +39,9 @@ SIGNATURES = {
     "sk_decode_attention_ex": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _I, _I, _P]),
     "sk_prefill_attention": (_I, [_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P]),
     "sk_decode_attention_noalloc": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P]),
+    "sk_decode_block_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "sk_decode_attention_block": (_I, [_P, _P, _F, _P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _I, _I,
+                                       _P, _SZ, _I, _P]),
 }
 
 _lib = None

@@ -9,6 +9,7 @@ DiT (engine/fused.py:293-298):
     dit_attention_layer — the whole block (producer, attention, gate) in two launches, bf16
 Qwen3 talker (qwen3/kernels.py:622-624):
     decode_attention  — one layer's decode step with the reference kernel's argument list
+    decode_attention_block — the layer's rms_gemv(qkv) -> attention -> gemv(o) in one launch
     prefill_attention — the prompt's causal attention (qwen3/fast.py:251-263), tensor cores
 """
 
@@ -329,6 +330,46 @@ def decode_attention(qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps:
     return out
 
 
+def decode_block_workspace(max_len: int, nq: int, nkv: int, device, hd: int = 128) -> torch.Tensor:
+    """A zero-filled workspace for decode_attention_block (allocate before graph capture)."""
+    n = int(lib().sk_decode_block_workspace_bytes(max_len, nq, nkv, hd))
+    return torch.zeros(max(n, 16), dtype=torch.uint8, device=device)
+
+
+def decode_attention_block(h: torch.Tensor, in_norm: torch.Tensor, eps_in: float, w_qkv: torch.Tensor,
+                           qn: torch.Tensor, kn: torch.Tensor, eps: float, rope: torch.Tensor, Kc: torch.Tensor,
+                           Vc: torch.Tensor, pos_ptr: torch.Tensor | None, pos_add: int, max_len: int, nq: int,
+                           nkv: int, w_o: torch.Tensor, workspace: torch.Tensor, kv_stable: bool = False) -> torch.Tensor:
+    """One talker layer's attention block in one launch (the reference's rms_gemv(qkv) -> attn -> gemv(o),
+    qwen3/kernels.py:619-624): h (fp32 [hidden]) += W_o · attn(W_qkv · RMSNorm(h) ⊙ in_norm), K/V appended
+    at pos = pos_ptr[0] + pos_add. Weights bf16 or fp32 (w_qkv [(nq+2nkv)·128][hidden], w_o [hidden][nq·128]);
+    caches bf16 or fp32 [nkv][max_len][128]. Returns h (updated in place)."""
+    hd = Kc.shape[-1]
+    hidden = h.numel()
+    for n, t in (("h", h), ("in_norm", in_norm), ("w_qkv", w_qkv), ("qn", qn), ("kn", kn), ("rope", rope), ("Kc", Kc),
+                 ("Vc", Vc), ("w_o", w_o), ("workspace", workspace)):
+        _cuda_contig(n, t)
+    _need(h.dtype == torch.float32 and in_norm.dtype == torch.float32 and in_norm.numel() == hidden,
+          "h and in_norm must be float32 [hidden]")
+    _need(w_qkv.dtype == w_o.dtype and w_qkv.dtype in (torch.bfloat16, torch.float32), "weights: one of bf16, fp32")
+    _need(w_qkv.numel() == (nq + 2 * nkv) * hd * hidden, "w_qkv must be [(nq+2nkv)*hd][hidden]")
+    _need(w_o.numel() == hidden * nq * hd, "w_o must be [hidden][nq*hd]")
+    _need(Kc.shape == Vc.shape and Kc.numel() == nkv * max_len * hd and Kc.dtype == Vc.dtype,
+          "Kc/Vc must be [nkv][max_len][hd]")
+    _need(rope.dtype == torch.float32 and rope.numel() >= max_len * hd, "rope must be float32 [max_len][hd]")
+    if pos_ptr is not None:
+        _need(pos_ptr.is_cuda and pos_ptr.dtype == torch.int64, "pos_ptr must be a CUDA int64 tensor")
+    ws_n = workspace.numel() * workspace.element_size()
+    with _nvtx("sk_decode_attention_block"):
+        check(lib().sk_decode_attention_block(_ptr(h), _ptr(in_norm), float(eps_in), _ptr(w_qkv), _ptr(qn), _ptr(kn),
+                                              float(eps), _ptr(rope), _ptr(Kc), _ptr(Vc), _ptr(pos_ptr), int(pos_add),
+                                              int(max_len), int(nq), int(nkv), int(hd), _ptr(w_o), int(hidden),
+                                              _dtype_code(w_qkv.dtype), _dtype_code(Kc.dtype), _ptr(workspace), ws_n,
+                                              _lib.SK_DECODE_KV_STABLE if kv_stable else 0, _stream()),
+              "sk_decode_attention_block")
+    return h
+
+
 def prefill_attention(qkv_rows: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps: float, rope: torch.Tensor,
                       Kc: torch.Tensor, Vc: torch.Tensor, pos0: int, max_len: int, nq: int, nkv: int,
                       out: torch.Tensor | None = None, q_buf: torch.Tensor | None = None) -> torch.Tensor:
@@ -364,4 +405,5 @@ def version() -> int:
 
 
 __all__ = ["dit_qkv_prologue", "dit_attention", "sdpa", "decode_attention", "decode_workspace",
+           "decode_attention_block", "decode_block_workspace",
            "decode_workspace_bytes", "device_error", "version", "_lib"]

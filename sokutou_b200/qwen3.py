@@ -37,6 +37,7 @@ class TalkerAttention:
         self.rope = rope_table(max_len, theta, hd, device)
         self.pos = torch.zeros((1,), dtype=torch.int64, device=device) if use_pos else None
         self.ws = ops.decode_workspace(max_len, nq, nkv, device, hd, cache_dtype)
+        self.block_ws = ops.decode_block_workspace(max_len, nq, nkv, device, hd)
 
     def attn(self, layer: int, qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, out: torch.Tensor,
              pos_add: int = 0, kv_stable: bool = False) -> torch.Tensor:
@@ -44,3 +45,12 @@ class TalkerAttention:
         after the layer's qkv projection; false right after the position advance)."""
         return ops.decode_attention(qkv, qn, kn, self.eps, self.rope, self.k[layer], self.v[layer], self.pos, pos_add,
                                     self.max_len, self.nq, self.nkv, out, self.ws, kv_stable)
+
+    def block(self, layer: int, h: torch.Tensor, in_norm: torch.Tensor, eps_in: float, w_qkv: torch.Tensor,
+              qn: torch.Tensor, kn: torch.Tensor, w_o: torch.Tensor, pos_add: int = 0,
+              kv_stable: bool = False) -> torch.Tensor:
+        """The layer's whole attention block — rms_gemv(qkv), the decode attention and gemv(o) into the
+        residual h (qwen3/kernels.py:619-624) — in one launch; h (fp32 [hidden]) is updated in place."""
+        return ops.decode_attention_block(h, in_norm, eps_in, w_qkv, qn, kn, self.eps, self.rope, self.k[layer],
+                                          self.v[layer], self.pos, pos_add, self.max_len, self.nq, self.nkv, w_o,
+                                          self.block_ws, kv_stable)

@@ -186,8 +186,11 @@ class SyntheticTalker:
         return {k: v.numpy() for k, v in self.w.items()}
 
     @torch.no_grad()
-    def generate(self, device, n_new: int, cache_dtype: torch.dtype = torch.float32, max_len: int | None = None):
-        """Greedy tokens of positions prompt-1 .. prompt-1+n_new through the B200 decode attention."""
+    def generate(self, device, n_new: int, cache_dtype: torch.dtype = torch.float32, max_len: int | None = None,
+                 fused: bool = False):
+        """Greedy tokens of positions prompt-1 .. prompt-1+n_new through the B200 decode attention; with
+        fused=True every layer's rms_gemv(qkv) -> attention -> gemv(o) runs as the one-launch block kernel
+        (input RMSNorm weight 1, fp32 weights) instead of torch projections around the attention."""
         from .qwen3 import TalkerAttention
 
         s = self.shape
@@ -195,12 +198,18 @@ class SyntheticTalker:
         max_len = max_len or (s.prompt + n_new)
         ta = TalkerAttention(s.n_layers, s.nq, s.nkv, max_len, s.theta, s.eps, device, cache_dtype, s.hd)
         att = torch.empty(s.nq * s.hd, device=device)
+        ones = torch.ones(s.hidden, device=device)
         rms = lambda h: h * torch.rsqrt((h * h).mean() + s.eps)
         tokens = []
         tok = None
         for pos in range(s.prompt + n_new):
             h = w["prompt"][pos] if pos < s.prompt else w["emb"][tok]
+            if fused:
+                h = h.clone()
             for li in range(s.n_layers):
+                if fused:
+                    ta.block(li, h, ones, s.eps, w["w_qkv"][li], w["qn"][li], w["kn"][li], w["w_o"][li])
+                    continue
                 qkv = (w["w_qkv"][li] @ rms(h)).contiguous()
                 ta.attn(li, qkv, w["qn"][li], w["kn"][li], att)
                 h = h + w["w_o"][li] @ att
