@@ -280,8 +280,10 @@ SK_API size_t sk_decode_block_workspace_bytes(int max_len, int nq, int nkv, int 
  *   flags    : 0 or SK_DECODE_KV_STABLE (the position and this layer's cache rows may be read before the
  *              kernel just before has finished; the weights are always prefetched before that wait)
  * One cooperative launch (one CTA per SM, all resident) with two grid-wide barriers between the
- * phases; no float atomics, so results are identical from run to run. hidden a multiple of 8; all
- * pointers 16-byte aligned; hd = 128, nq = 2*nkv.
+ * phases; no float atomics, so results are identical from run to run. hidden a multiple of 8 and at
+ * most 2048 (nq * hd at most 2048); the attention's partials of every 128-key chunk must fit one CTA's
+ * shared memory (nkv = 8: max_len up to 3328), else SK_ERR_UNSUPPORTED; all pointers 16-byte aligned;
+ * hd = 128, nq = 2*nkv.
  */
 SK_API int sk_decode_attention_block(float* h, const float* in_norm, float eps_in, const void* w_qkv,
                                      const float* qn, const float* kn, float eps, const float* rope,
