@@ -731,6 +731,70 @@ def dit_gemm(device, dist: Dist, calls: int = 60, sets: int = 4) -> dict:
     return out
 
 
+# ------------------------------------------------------------------------------- grouped decode requests
+def c3_grouped(device, dist: Dist, Rs=(8, 32), lo: int = 1023, hi: int = 1120) -> dict:
+    """c3-shaped decode attention for R independent talkers in one launch per layer
+    (sk_decode_attention_grouped): R requests x 28 layers, positions lo..hi-1 (T >= 1024), each request with
+    its own caches (R x 176 MB, far past L2), graph-replayed one decode step (28 grouped launches and the
+    position advances) at a time. Bytes per launch: R times the one-request algorithmic bytes."""
+    from sokutou_b200 import ops, qwen3, workloads as W
+    s = W.C3
+    out = {}
+    for R in Rs:
+        g = torch.Generator(device=device).manual_seed(R)
+        tas = []
+        for _ in range(R):
+            ta = qwen3.TalkerAttention(s.n_layers, s.nq, s.nkv, 1152, s.theta, s.eps, device, torch.bfloat16)
+            ta.k.normal_(generator=g)
+            ta.v.normal_(generator=g)
+            tas.append(ta)
+        qkv = torch.randn(R, s.n_layers, (s.nq + 2 * s.nkv) * s.hd, device=device, generator=g)
+        qn = 1 + 0.02 * torch.randn(s.n_layers, s.hd, device=device, generator=g)
+        att = torch.empty(R, s.n_layers, s.nq * s.hd, device=device)
+        descs = [ops.decode_requests([{"qkv": qkv[r, li], "qn": qn[li], "kn": qn[li], "rope": tas[r].rope,
+                                       "Kc": tas[r].k[li], "Vc": tas[r].v[li], "pos_ptr": tas[r].pos,
+                                       "out": att[r, li], "pos_add": 0, "eps": s.eps} for r in range(R)], device)
+                 for li in range(s.n_layers)]
+
+        def step():
+            for li in range(s.n_layers):
+                ops.decode_attention_grouped(descs[li], R, 1152, s.nq, s.nkv, torch.bfloat16, kv_stable=li > 0)
+            for ta in tas:
+                ta.pos.add_(1)
+
+        st = torch.cuda.Stream(device)
+        st.wait_stream(torch.cuda.current_stream(device))
+        for ta in tas:
+            ta.pos.fill_(lo)
+        with torch.cuda.stream(st):
+            step()
+        torch.cuda.current_stream(device).wait_stream(st)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            step()
+        for ta in tas:
+            ta.pos.fill_(lo)
+        gr.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        for ta in tas:
+            ta.pos.fill_(lo)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(lo, hi):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = dist.max(e0.elapsed_time(e1))
+        del gr
+        tot = R * s.n_layers * sum(s.layer_bytes(p + 1) for p in range(lo, hi))
+        out[f"R{R}"] = {"us_per_launch": round(ms * 1e3 / ((hi - lo) * s.n_layers), 3),
+                        "gbs": round(tot / (ms / 1e3) / 1e9, 1), "requests": R, "T_range": [lo + 1, hi]}
+        del tas, descs
+        torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------------------- fused decode layer block
 def decode_block_bench(device, dist: Dist, hidden: int = 2048, lo: int = 1023, hi: int = 1120) -> dict:
     """One talker layer's attention block — rms_gemv(qkv) -> attention -> gemv(o), the three launches of
@@ -883,7 +947,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-serving", action="store_true")
     ap.add_argument("--only-c1", action="store_true", help="headline workload only (for launch-list captures)")
-    ap.add_argument("--skip", default="", help="comma list of extra sections to leave out: sdpa,layer,gemm,prefill,block,serving")
+    ap.add_argument("--skip", default="", help="comma list of extra sections to leave out: sdpa,layer,gemm,prefill,block,grouped,serving")
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU time budget of the reference arm")
     a = ap.parse_args()
     if a.impl == "reference":
@@ -970,6 +1034,10 @@ def main():
     gemm = None if "gemm" in skip else dit_gemm(dev, dist)
     prefill = None if "prefill" in skip else prefill_bench(dev, dist)
     dblock = None if "block" in skip else decode_block_bench(dev, dist)
+    grouped = None if "grouped" in skip else c3_grouped(dev, dist)
+    if grouped:
+        for v in grouped.values():
+            v["frac_of_measured_hbm"] = round(v["gbs"] / pk["hbm_gbs"], 4)
     if dblock:
         dblock["fused_frac_of_measured_hbm"] = round(dblock["fused_gbs"] / pk["hbm_gbs"], 4)
 
@@ -998,7 +1066,7 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": UNIT,
                          "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk_kind} bf16 burst",
                          "frac_of_spec": round(achieved / SPEC["bf16_tflops"], 4), "traffic": traffic},
-            "c2": c2_res, "c3": c3_res, "sdpa_gpu": sdpa, "layer_block": blocks, "dit_gemm": gemm, "prefill": prefill, "decode_block": dblock, "serving": serv, "cpu_baseline": cpu,
+            "c2": c2_res, "c3": c3_res, "sdpa_gpu": sdpa, "layer_block": blocks, "dit_gemm": gemm, "prefill": prefill, "decode_block": dblock, "c3_grouped": grouped, "serving": serv, "cpu_baseline": cpu,
             "clocks": clk.summary(), "device_error": err,
         }
         print(json.dumps(line), flush=True)

@@ -259,6 +259,40 @@ SK_API int sk_prefill_attention(const float* qkv, const float* qn, const float* 
                                 int nq, int nkv, int hd, void* out, void* q_buf, int cache_dtype,
                                 void* stream);
 
+/*
+ * One independent decode request of sk_decode_attention_grouped: the scalar arguments of
+ * sk_decode_attention for one talker (its qkv, norms, RoPE table, this layer's caches, its position on
+ * the device and its output). 80 bytes; an array of them lives in device memory.
+ */
+typedef struct SkDecodeRequest {
+  const float* qkv;          /* [(nq + 2*nkv) * hd] */
+  const float* qn;           /* [hd] */
+  const float* kn;           /* [hd] */
+  const float* rope;         /* [max_len][hd] */
+  void* Kc;                  /* [nkv][max_len][hd], cache_dtype */
+  void* Vc;
+  const long long* pos_ptr;  /* the request's position on the device (NULL: pos = pos_add) */
+  float* out;                /* [nq * hd] */
+  int pos_add;
+  float eps;
+  int reserved[2];
+} SkDecodeRequest;
+
+/*
+ * R independent decode requests in one launch: request r does what sk_decode_attention does with the
+ * arguments in reqs[r] — the same appended cache rows, and the output of its thread-block-cluster kernel
+ * (the same bits where sk_decode_attention runs that kernel too; within rounding where it falls back
+ * to its split-KV workspace kernel) — all sharing max_len, nq, nkv, hd and the cache dtype. No counterpart in the reference, which serves one request at a time (README.md:186): a server
+ * holding several talkers' decodes in flight gets one launch per layer for all of them instead of one
+ * per request, and so moves R times the cache bytes per launch.
+ *   reqs  : DEVICE pointer to R descriptors (filled before capture; they are read on the device)
+ *   flags : 0 or SK_DECODE_KV_STABLE, as sk_decode_attention_ex (for every request)
+ * Caches must be short enough for the cluster kernel (bf16: max_len up to 5040; fp32: 2528), else
+ * SK_ERR_UNSUPPORTED. Positions out of range set SK_DEVERR_POS_RANGE and skip that request.
+ */
+SK_API int sk_decode_attention_grouped(const SkDecodeRequest* reqs, int R, int max_len, int nq, int nkv, int hd,
+                                       int cache_dtype, int flags, void* stream);
+
 /* Bytes of workspace sk_decode_attention_block needs for caches of max_len positions. */
 SK_API size_t sk_decode_block_workspace_bytes(int max_len, int nq, int nkv, int hd);
 

@@ -40,9 +40,20 @@ SIGNATURES = {
     "sk_prefill_attention": (_I, [_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P]),
     "sk_decode_attention_noalloc": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P]),
     "sk_decode_block_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "sk_decode_attention_grouped": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "sk_decode_attention_block": (_I, [_P, _P, _F, _P, _P, _P, _F, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _I, _I,
                                        _P, _SZ, _I, _P]),
 }
+
+
+
+class SkDecodeRequest(ctypes.Structure):
+    """include/sokutou_b200.h SkDecodeRequest (80 bytes): one request of sk_decode_attention_grouped."""
+    _fields_ = [("qkv", _P), ("qn", _P), ("kn", _P), ("rope", _P), ("Kc", _P), ("Vc", _P), ("pos_ptr", _P),
+                ("out", _P), ("pos_add", _I), ("eps", _F), ("reserved", _I * 2)]
+
+
+assert ctypes.sizeof(SkDecodeRequest) == 80
 
 _lib = None
 

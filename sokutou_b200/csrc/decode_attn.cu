@@ -413,11 +413,39 @@ constexpr int kPartialBytes = kG * kHD * 4 + kG * 2 * 4;  // one CTA's (o, max, 
 // EARLY: the position and this layer's cache rows before it are not written by the kernel launched
 // just before this one, so the position is read and the K/V chunk copies are issued before
 // griddepcontrol.wait — they overlap that kernel's tail; only qkv, qn and kn wait for it.
-template <typename CT, bool EARLY>
+// GROUPED: one launch decodes the independent requests reqs[0 .. gridDim.z): blockIdx.z picks the
+// request whose qkv, norms, RoPE table, caches, position and output replace the scalar arguments; every
+// request shares max_len, nq, nkv and the cache type. The descriptors are read before the wait for the
+// kernel ahead (the caller fills them before capture and does not change them between launches).
+template <typename CT, bool EARLY, bool GROUPED = false>
 __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
-    const float* __restrict__ qkv, const float* __restrict__ qn, const float* __restrict__ kn, float eps,
-    const float* __restrict__ rope, CT* __restrict__ Kc, CT* __restrict__ Vc, const long long* __restrict__ pos_ptr,
-    int pos_add, int max_len, int nq, int nkv, float* __restrict__ out, int* err) {
+    const float* __restrict__ qkv_a, const float* __restrict__ qn_a, const float* __restrict__ kn_a, float eps_a,
+    const float* __restrict__ rope_a, CT* __restrict__ Kc_a, CT* __restrict__ Vc_a,
+    const long long* __restrict__ pos_ptr_a, int pos_add_a, int max_len, int nq, int nkv, float* __restrict__ out_a,
+    int* err, const SkDecodeRequest* __restrict__ reqs) {
+  const float* qkv = qkv_a;
+  const float* qn = qn_a;
+  const float* kn = kn_a;
+  float eps = eps_a;
+  const float* rope = rope_a;
+  CT* Kc = Kc_a;
+  CT* Vc = Vc_a;
+  const long long* pos_ptr = pos_ptr_a;
+  int pos_add = pos_add_a;
+  float* out = out_a;
+  if (GROUPED) {
+    const SkDecodeRequest& r = reqs[blockIdx.z];
+    qkv = r.qkv;
+    qn = r.qn;
+    kn = r.kn;
+    eps = r.eps;
+    rope = r.rope;
+    Kc = reinterpret_cast<CT*>(r.Kc);
+    Vc = reinterpret_cast<CT*>(r.Vc);
+    pos_ptr = r.pos_ptr;
+    pos_add = r.pos_add;
+    out = r.out;
+  }
   const int CL = (int)cluster_size_reg();
   const int rank = (int)cluster_rank();
   const int chunk_max = (max_len + CL - 1) / CL;
@@ -781,12 +809,80 @@ static int launch_cluster(const float* qkv, const float* qn, const float* kn, fl
     const cudaError_t e =
         early ? cudaLaunchKernelEx(&cfg, decode_attn_cluster_kernel<CT, true>, qkv, qn, kn, eps, rope,
                                    reinterpret_cast<CT*>(Kc), reinterpret_cast<CT*>(Vc), pos_ptr, pos_add, max_len, nq,
-                                   nkv, out, err)
+                                   nkv, out, err, (const SkDecodeRequest*)nullptr)
               : cudaLaunchKernelEx(&cfg, decode_attn_cluster_kernel<CT, false>, qkv, qn, kn, eps, rope,
                                    reinterpret_cast<CT*>(Kc), reinterpret_cast<CT*>(Vc), pos_ptr, pos_add, max_len, nq,
-                                   nkv, out, err);
+                                   nkv, out, err, (const SkDecodeRequest*)nullptr);
     if (e != cudaSuccess) return SK_ERR_CUDA;
     return SK_OK;
+  }
+  return SK_ERR_UNSUPPORTED;
+}
+
+template <typename CT>
+static int launch_grouped(const SkDecodeRequest* reqs, int R, int max_len, int nq, int nkv, int* err, bool early,
+                          cudaStream_t st) {
+  for (int cl : {16, 8}) {
+    const int chunk_max = (max_len + cl - 1) / cl;
+    const size_t smem = 2 * (size_t)chunk_max * kHD * sizeof(CT) + (size_t)kG * ((chunk_max + 63) & ~63) * 4;
+    if (smem > 160 * 1024) continue;
+    auto kern = early ? decode_attn_cluster_kernel<CT, true, true> : decode_attn_cluster_kernel<CT, false, true>;
+    cudaLaunchConfig_t cfg = {};
+    {
+      // the clusters of a grouped launch depend on nothing outside themselves: they may run wave after
+      // wave, so one schedulable cluster of this size is enough (cached per device, mode and size)
+      static std::mutex mu;
+      static size_t set_to[64][2] = {};
+      static int ok_cl[64][2] = {};
+      static size_t ok_smem[64][2] = {};
+      int dev = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SK_ERR_CUDA;
+      std::lock_guard<std::mutex> lk(mu);
+      if (set_to[dev][early] < smem) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+          return SK_ERR_CUDA;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        set_to[dev][early] = smem;
+      }
+      if (ok_smem[dev][early] != smem || ok_cl[dev][early] != cl) {
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3(cl, nkv);
+        q.blockDim = dim3(kThreadsCl);
+        q.dynamicSmemBytes = smem;
+        cudaLaunchAttribute a[1];
+        a[0].id = cudaLaunchAttributeClusterDimension;
+        a[0].val.clusterDim.x = cl;
+        a[0].val.clusterDim.y = 1;
+        a[0].val.clusterDim.z = 1;
+        q.attrs = a;
+        q.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n < 1) {
+          cudaGetLastError();  // clear a refused query
+          continue;
+        }
+        ok_cl[dev][early] = cl;
+        ok_smem[dev][early] = smem;
+      }
+    }
+    cfg.gridDim = dim3(cl, nkv, R);
+    cfg.blockDim = dim3(kThreadsCl);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, kern, (const float*)nullptr, (const float*)nullptr, (const float*)nullptr, 0.f,
+                           (const float*)nullptr, (CT*)nullptr, (CT*)nullptr, (const long long*)nullptr, 0, max_len,
+                           nq, nkv, (float*)nullptr, err, reqs) != cudaSuccess)
+      return SK_ERR_CUDA;
+    return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
   }
   return SK_ERR_UNSUPPORTED;
 }
@@ -952,4 +1048,21 @@ int sk_launch_prefill_prologue(const float* qkv, const float* qn, const float* k
                                reinterpret_cast<float*>(q_buf), pos0, T, max_len, nq, nkv, err);
   if (e != cudaSuccess) return SK_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
+}
+
+extern "C" int sk_decode_attention_grouped(const SkDecodeRequest* reqs, int R, int max_len, int nq, int nkv, int hd,
+                                           int cache_dtype, int flags, void* stream) {
+  if (flags & ~SK_DECODE_KV_STABLE) return SK_ERR_INVALID_ARG;
+  if (!reqs || R <= 0 || R > 65535 || max_len <= 0 || nkv <= 0 || nq <= 0) return SK_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(reqs) & 15) return SK_ERR_INVALID_ARG;
+  if (hd != decode::kHD || nq != decode::kG * nkv) return SK_ERR_UNSUPPORTED;
+  if (cache_dtype != SK_BF16 && cache_dtype != SK_F32) return SK_ERR_UNSUPPORTED;
+  int rc = sk_check_device();
+  if (rc != SK_OK) return rc;
+  int* err = sk_error_word_ptr();
+  if (!err) return SK_ERR_CUDA;
+  const bool early = (flags & SK_DECODE_KV_STABLE) != 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return cache_dtype == SK_BF16 ? decode::launch_grouped<__nv_bfloat16>(reqs, R, max_len, nq, nkv, err, early, st)
+                                : decode::launch_grouped<float>(reqs, R, max_len, nq, nkv, err, early, st);
 }

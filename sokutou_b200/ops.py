@@ -330,6 +330,38 @@ def decode_attention(qkv: torch.Tensor, qn: torch.Tensor, kn: torch.Tensor, eps:
     return out
 
 
+def decode_requests(reqs: list[dict], device) -> torch.Tensor:
+    """The device array of SkDecodeRequest descriptors for decode_attention_grouped, one per dict with the
+    tensors qkv, qn, kn, rope, Kc, Vc, out, the optional pos_ptr (CUDA int64) and the ints/floats pos_add,
+    eps. Build it before graph capture and keep the tensors alive while it is used."""
+    arr = (_lib.SkDecodeRequest * len(reqs))()
+    for i, r in enumerate(reqs):
+        for n in ("qkv", "qn", "kn", "rope", "Kc", "Vc", "out"):
+            _cuda_contig(n, r[n])
+        _need(r["qkv"].dtype == torch.float32 and r["out"].dtype == torch.float32, "qkv and out must be float32")
+        pp = r.get("pos_ptr")
+        if pp is not None:
+            _need(pp.is_cuda and pp.dtype == torch.int64, "pos_ptr must be a CUDA int64 tensor")
+        arr[i] = _lib.SkDecodeRequest(_ptr(r["qkv"]), _ptr(r["qn"]), _ptr(r["kn"]), _ptr(r["rope"]), _ptr(r["Kc"]),
+                                      _ptr(r["Vc"]), _ptr(pp), _ptr(r["out"]), int(r.get("pos_add", 0)),
+                                      float(r["eps"]), (ctypes.c_int * 2)(0, 0))
+    host = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
+    return host.to(device)
+
+
+def decode_attention_grouped(reqs_dev: torch.Tensor, n: int, max_len: int, nq: int, nkv: int,
+                             cache_dtype: torch.dtype = torch.bfloat16, kv_stable: bool = False) -> None:
+    """n independent decode requests (descriptors from decode_requests) in one launch: each does exactly what
+    decode_attention does with its own arguments; all share max_len, nq, nkv and the cache dtype."""
+    _need(reqs_dev.is_cuda and reqs_dev.dtype == torch.uint8 and reqs_dev.numel() >= 80 * n,
+          "reqs_dev must be the device descriptor array of decode_requests")
+    with _nvtx("sk_decode_attention_grouped"):
+        check(lib().sk_decode_attention_grouped(_ptr(reqs_dev), int(n), int(max_len), int(nq), int(nkv), 128,
+                                                _dtype_code(cache_dtype),
+                                                _lib.SK_DECODE_KV_STABLE if kv_stable else 0, _stream()),
+              "sk_decode_attention_grouped")
+
+
 def decode_block_workspace(max_len: int, nq: int, nkv: int, device, hd: int = 128) -> torch.Tensor:
     """A zero-filled workspace for decode_attention_block (allocate before graph capture)."""
     n = int(lib().sk_decode_block_workspace_bytes(max_len, nq, nkv, hd))
@@ -405,5 +437,5 @@ def version() -> int:
 
 
 __all__ = ["dit_qkv_prologue", "dit_attention", "sdpa", "decode_attention", "decode_workspace",
-           "decode_attention_block", "decode_block_workspace",
+           "decode_attention_block", "decode_block_workspace", "decode_attention_grouped", "decode_requests",
            "decode_workspace_bytes", "device_error", "version", "_lib"]
