@@ -925,17 +925,17 @@ def serving(dist: Dist, device):
     ex.warm(mine)
     torch.cuda.synchronize()
     dist.barrier()
-    t0 = time.perf_counter()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for r in mine:
-        ex.run(r)
+    ex.run_all(mine)
     e1.record()
     torch.cuda.synchronize()
     dt = dist.max(e0.elapsed_time(e1) / 1e3)
     dist.barrier()
     return {"requests": len(reqs), "sentences_per_s": len(reqs) / dt, "makespan_s": dt,
-            "per_rank_requests": [len(p) for p in plan], "sharding": "longest-first static, no collectives"}
+            "per_rank_requests": [len(p) for p in plan], "sharding": "longest-first static, no collectives",
+            "decode": f"continuous batching over {SV.GpuExecutor.SLOTS} slots, one grouped launch per layer",
+            "dit_inputs": "distinct q/k/v per call from a pool larger than L2"}
 
 
 # ---------------------------------------------------------------------------------------------- main

@@ -43,7 +43,8 @@ def cost_estimate(r: Request) -> float:
         calls = [3] * 240 + [1] * 240
         return sum(4 * B * 16 * r.size * K * 128 / 5e14 + 5e-6 for B in calls)
     steps = max(r.size - 96, 0)
-    return sum(28 * (2 * 8 * (96 + i) * 128 * 2 / 1.5e12 + 3e-6) for i in range(1, steps + 1))
+    # decodes share grouped launches (GpuExecutor.SLOTS talkers per launch): ~2 TB/s, ~2.5 us per layer each
+    return sum(28 * (2 * 8 * (96 + i) * 128 * 2 / 2e12 + 2.5e-6) for i in range(1, steps + 1))
 
 
 def plan_lpt(reqs: list[Request], n: int) -> list[list[Request]]:
@@ -175,6 +176,7 @@ class GpuExecutor:
         self.max_cache = max_cache
         self.dit = {}       # L -> (graph, buffers)
         self.dec = None     # (graph, TalkerAttention, buffers)
+        self.slots = None   # (graph, talkers, buffers) of the continuous-batching decode slots
 
     # Distinct q/k/v per attention call, as in the engine (each layer and step reads new projections):
     # a pool of flat buffers larger than L2, rotated over the calls of every request, so no request
@@ -266,6 +268,8 @@ class GpuExecutor:
                 self.dit[r.size] = self._dit_graph(r.size)
             elif r.kind == "decode" and self.dec is None:
                 self.dec = self._decode_graph()
+        if any(r.kind == "decode" for r in reqs) and self.slots is None:
+            self.slots = self._decode_slots()
 
     def run(self, r: Request):
         self.warm([r])
@@ -276,3 +280,78 @@ class GpuExecutor:
             ta.pos.fill_(96)
             for _ in range(96, min(r.size, self.max_cache)):
                 gr.replay()
+
+    # ---- continuous batching of decode requests -------------------------------------------------
+    # SLOTS talkers decode side by side, one grouped launch per layer for all of them
+    # (sk_decode_attention_grouped): every step advances every slot by one position; a slot whose
+    # request has reached its final length takes the next waiting request (its position reset to the
+    # prompt length). Requests are handed out longest first, so the slots finish close together.
+    SLOTS = 8
+
+    def _decode_slots(self):
+        import torch
+
+        from . import ops, qwen3, workloads as W
+        s, R = W.C3, self.SLOTS
+        g = torch.Generator(device=self.device).manual_seed(5)
+        tas = []
+        for _ in range(R):
+            ta = qwen3.TalkerAttention(s.n_layers, s.nq, s.nkv, self.max_cache, s.theta, s.eps, self.device,
+                                       torch.bfloat16)
+            ta.k.normal_(generator=g)
+            ta.v.normal_(generator=g)
+            tas.append(ta)
+        qkv = torch.randn(R, s.n_layers, (s.nq + 2 * s.nkv) * s.hd, device=self.device, generator=g)
+        qn = 1 + 0.02 * torch.randn(s.n_layers, s.hd, device=self.device, generator=g)
+        out = torch.empty(R, s.n_layers, s.nq * s.hd, device=self.device)
+        descs = [ops.decode_requests([{"qkv": qkv[r, li], "qn": qn[li], "kn": qn[li], "rope": tas[r].rope,
+                                       "Kc": tas[r].k[li], "Vc": tas[r].v[li], "pos_ptr": tas[r].pos,
+                                       "out": out[r, li], "pos_add": 0, "eps": s.eps} for r in range(R)], self.device)
+                 for li in range(s.n_layers)]
+
+        def step():
+            for li in range(s.n_layers):
+                ops.decode_attention_grouped(descs[li], R, self.max_cache, s.nq, s.nkv, torch.bfloat16,
+                                             kv_stable=li > 0)
+            for ta in tas:
+                ta.pos.add_(1)
+
+        for ta in tas:
+            ta.pos.fill_(96)
+        gr = self._capture(step)
+        return gr, tas, (qkv, qn, out, descs)
+
+    def run_decodes(self, reqs: list[Request]) -> int:
+        """Every decode request of `reqs` through the slots; returns the number of steps replayed."""
+        self.warm(reqs)
+        gr, tas, _ = self.slots
+        queue = sorted(reqs, key=lambda r: -r.size)
+        left = [0] * self.SLOTS  # steps the slot's current request still needs
+        for i, ta in enumerate(tas):
+            if queue:
+                r = queue.pop(0)
+                left[i] = max(0, min(r.size, self.max_cache) - 96)
+                ta.pos.fill_(96)
+        steps = 0
+        while any(left):
+            n = min(x for x in left if x > 0)  # replays until the next slot finishes
+            for _ in range(n):
+                gr.replay()
+            steps += n
+            for i, ta in enumerate(tas):
+                if left[i] > 0:
+                    left[i] -= n
+                    if left[i] == 0 and queue:
+                        r = queue.pop(0)
+                        left[i] = max(0, min(r.size, self.max_cache) - 96)
+                        ta.pos.fill_(96)
+        return steps
+
+    def run_all(self, reqs: list[Request]) -> None:
+        """A rank's share of the sweep: its DiT syntheses one after another, its decodes through the slots."""
+        for r in reqs:
+            if r.kind == "dit":
+                self.run(r)
+        dec = [r for r in reqs if r.kind == "decode"]
+        if dec:
+            self.run_decodes(dec)
