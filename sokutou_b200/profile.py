@@ -2,6 +2,7 @@
 
     python -m sokutou_b200.profile --case dit_c1_L512_b3 [--reps 50] [--graph]
     python -m sokutou_b200.profile --case decode_T1120 [--reps 50] [--graph]
+    python -m sokutou_b200.profile --case block_T1120 [--reps 50] [--graph]
 
 Prints one JSON record: the case's shape, average microseconds per call from CUDA events over `reps`
 back-to-back calls (eager launches, or one CUDA graph holding them with --graph), the algorithmic work
@@ -43,6 +44,10 @@ CASES = {
     "linear_c2_o_b3": ("linear", (1536, 2048, 2048), "sk"), "cublas_c2_o_b3": ("linear", (1536, 2048, 2048), "cublas"),
     "linear_fp8_c2_qkvg_b3": ("linear", (1536, 8192, 2048), "sk_fp8"),
     "scaledmm_c2_qkvg_b3": ("linear", (1536, 8192, 2048), "cublas_fp8"),
+    # one talker layer's attention block in one launch (rms_gemv(qkv) -> attention -> gemv(o)), 1.7B width
+    "block_T1120": ("block", 1120, 2048), "block_T128": ("block", 128, 2048),
+    # R independent decode requests in one launch
+    "grouped_R8_T1120": ("grouped", 1120, 8), "grouped_R32_T1120": ("grouped", 1120, 32),
     # calibration: what a chain of dependent kernels costs on this GPU without any attention work
     "calib_tiny": ("calib", 0, None), "calib_copy_4.6MB": ("calib", 4616192, None),
 }
@@ -133,6 +138,55 @@ def decode_case(T, sets, dev, kv_stable=False):
     return fns, s.layer_bytes(T), "byte"
 
 
+def block_case(T, hidden, sets, dev):
+    """One talker layer's attention block (sk_decode_attention_block) at T keys, bf16 weights and cache;
+    work = both weight matrices + the decode attention's bytes + the h / qkv / att traffic."""
+    s = W.C3
+    max_len = 1536
+    g = torch.Generator(device=dev).manual_seed(0)
+    Dq = (s.nq + 2 * s.nkv) * s.hd
+    fns = []
+    for _ in range(sets):
+        ta = qwen3.TalkerAttention(1, s.nq, s.nkv, max_len, s.theta, s.eps, dev, torch.bfloat16)
+        ta.k.normal_(generator=g)
+        ta.v.normal_(generator=g)
+        ta.pos.fill_(T - 1)
+        wq = (torch.randn(Dq, hidden, device=dev, generator=g) / hidden ** 0.5).bfloat16()
+        wo = (torch.randn(hidden, s.nq * s.hd, device=dev, generator=g) / (s.nq * s.hd) ** 0.5).bfloat16()
+        h = torch.randn(hidden, device=dev, generator=g)
+        nw = torch.ones(hidden, device=dev)
+        qn = torch.ones(s.hd, device=dev)
+        # the position stays at T - 1: every call re-appends the same row and attends over T keys
+        fns.append(lambda ta=ta, wq=wq, wo=wo, h=h, nw=nw, qn=qn: ta.block(0, h, nw, s.eps, wq, qn, qn, wo))
+    return fns, (Dq + hidden) * hidden * 2 + s.layer_bytes(T) + 2 * hidden * 4, "byte"
+
+
+def grouped_case(T, R, sets, dev):
+    """R independent decode requests at T keys in one launch (sk_decode_attention_grouped); work = R times
+    the one-request bytes."""
+    s = W.C3
+    max_len = 1152
+    g = torch.Generator(device=dev).manual_seed(0)
+    fns = []
+    for _ in range(sets):
+        tas = []
+        for _ in range(R):
+            ta = qwen3.TalkerAttention(1, s.nq, s.nkv, max_len, s.theta, s.eps, dev, torch.bfloat16)
+            ta.k.normal_(generator=g)
+            ta.v.normal_(generator=g)
+            ta.pos.fill_(T - 1)
+            tas.append(ta)
+        qkv = torch.randn(R, (s.nq + 2 * s.nkv) * s.hd, device=dev, generator=g)
+        qn = torch.ones(s.hd, device=dev)
+        out = torch.empty(R, s.nq * s.hd, device=dev)
+        descs = ops.decode_requests([{"qkv": qkv[r], "qn": qn, "kn": qn, "rope": tas[r].rope, "Kc": tas[r].k[0],
+                                      "Vc": tas[r].v[0], "pos_ptr": tas[r].pos, "out": out[r], "eps": s.eps}
+                                     for r in range(R)], dev)
+        keep = (tas, qkv, qn, out)
+        fns.append(lambda descs=descs, keep=keep: ops.decode_attention_grouped(descs, R, max_len, s.nq, s.nkv))
+    return fns, R * s.layer_bytes(T), "byte"
+
+
 def linear_case(mnk, impl, sets, dev):
     """y = x·wᵀ (engine/fused.py:262-264) on sk_dit_linear or on torch's F.linear (cuBLAS); work = 2·M·N·K."""
     M, N, K = mnk
@@ -195,6 +249,10 @@ def main():
         fns, work, unit = linear_case(x, B, a.sets, dev)
     elif kind == "decode":
         fns, work, unit = decode_case(x, a.sets, dev, kv_stable=(B == "kv_stable"))
+    elif kind == "block":
+        fns, work, unit = block_case(x, B, a.sets, dev)
+    elif kind == "grouped":
+        fns, work, unit = grouped_case(x, B, a.sets, dev)
     else:
         fns, work, unit = calib_case(x, a.sets, dev)
     for f in fns:
@@ -244,9 +302,14 @@ def _shape(kind, x, B):
         return {"B": B, "H": x.H, "hd": x.hd, "L": x.L, "text_keys": x.Tb, "speaker_keys": x.Sp}
     if kind == "linear":
         return {"M": x[0], "N": x[1], "K": x[2], "impl": B}
-    if kind in ("decode", "prefill"):
+    if kind in ("decode", "prefill", "block", "grouped"):
         s = W.C3
-        return {"T": x, "nq": s.nq, "nkv": s.nkv, "hd": s.hd}
+        d = {"T": x, "nq": s.nq, "nkv": s.nkv, "hd": s.hd}
+        if kind == "block":
+            d["hidden"] = B
+        if kind == "grouped":
+            d["requests"] = B
+        return d
     return {"bytes": x}
 
 

@@ -20,7 +20,8 @@ def test_parity_suites_under_bounds_checks(cuda):
     lib = build.build(checked=True)
     env = dict(os.environ, SOKUTOU_B200_LIB=lib, SOKUTOU_B200_CHECK_BOUNDS="1")
     suites = ["tests/test_dit_gpu.py", "tests/test_layer_gpu.py", "tests/test_gate_gpu.py", "tests/test_decode_gpu.py",
-              "tests/test_linear_gpu.py", "tests/test_zz_no_alloc.py"]
+              "tests/test_linear_gpu.py", "tests/test_decode_block_gpu.py", "tests/test_decode_grouped_gpu.py",
+              "tests/test_zz_no_alloc.py"]
     r = subprocess.run([sys.executable, "-m", "pytest", *suites, "-m", "gpu", "-q", "-x", "-p", "no:cacheprovider",
                         "-k", "not greedy"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
     tail = "\n".join((r.stdout + r.stderr).strip().splitlines()[-15:])
