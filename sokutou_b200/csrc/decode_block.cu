@@ -6,8 +6,9 @@
 // which the reference runs as three launches per layer (qwen3/kernels.py:619-624).
 //
 // Each of the three steps needs the whole output of the one before, so the launch is cooperative: one
-// CTA per SM, all resident, with two grid-wide barriers between the phases (a counter and a generation
-// word in the caller's workspace; bounded spins that record SK_DEVERR_TIMEOUT and give up after 2 s).
+// CTA per SM, all resident, with two grid-wide barriers between the phases (two monotonic counters in
+// the caller's workspace — arrivals and completed barriers, never reset, read once per launch; bounded
+// spins that record SK_DEVERR_TIMEOUT and give up after 2 s).
 // The weights do not depend on anything computed in the launch: each CTA's W_qkv rows are fetched into
 // its shared memory by one bulk copy issued before the launch waits for the kernel ahead of it; once
 // they have landed the W_o rows and the K/V chunks are asked into L2, so that they stream from HBM
