@@ -25,7 +25,7 @@ LIB = os.path.join(LIB_DIR, "libsokutou_b200.so")
 LIB_CHECKED = os.path.join(LIB_DIR, "libsokutou_b200_checked.so")
 SOURCES = ["api.cu", "decode_attn.cu", "dit_prologue.cu", "dit_attn_f32.cu", "dit_attn_tc.cu", "dit_gate.cu",
            "dit_linear.cu", "decode_block.cu"]
-HEADERS = ["sk_common.cuh", "dit_qk_math.cuh"]
+HEADERS = ["sk_common.cuh", "dit_qk_math.cuh", "dit_attn_tc.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr"]

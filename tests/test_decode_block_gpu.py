@@ -198,3 +198,31 @@ def test_block_errors(cuda):
     torch.cuda.synchronize()
     assert rel_l2(host(d["h"]), want) <= BF16_TOL
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("wdt,cdt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16)])
+def test_code_predictor_form_positions_from_pos_add(cuda, wdt, cdt):
+    """The code predictor's call form (qwen3/kernels.py:600-617, `_layers(C, ..., pos_ptr=None,
+    pos_add=g)`): no device position, the write index is pos_add itself, a 16-row cache
+    (max_len = G = 16) filled position by position 0..15, a 1024-wide hidden state. Every step against the
+    float64 oracle, which appends to its own copy of the caches."""
+    max_len, hidden = 16, 1024
+    d = _case(cuda, hidden, max_len, 1, wdt, cdt, seed=31)
+    d["Kc"].zero_()
+    d["Vc"].zero_()
+    Kh, Vh = host(d["Kc"]), host(d["Vc"])
+    ws = ops.decode_block_workspace(max_len, 16, 8, cuda)
+    tol = FP32_TOL if (wdt, cdt) == (torch.float32, torch.float32) else BF16_TOL
+    for g in range(max_len):
+        want = Q.decode_block(host(d["h"]), host(d["in_norm"]), 1e-6, host(d["w_qkv"]), host(d["qn"]), host(d["kn"]),
+                              1e-6, d["rope"].cpu().numpy(), Kh, Vh, g, 16, 8, host(d["w_o"]),
+                              "bf16" if cdt == torch.bfloat16 else "f32")
+        ops.decode_attention_block(d["h"], d["in_norm"], 1e-6, d["w_qkv"], d["qn"], d["kn"], 1e-6, d["rope"], d["Kc"],
+                                   d["Vc"], None, g, max_len, 16, 8, d["w_o"], ws)
+        torch.cuda.synchronize()
+        assert rel_l2(host(d["h"]), want) <= tol, g
+        # the next step starts from the same state on both sides: the oracle's h, the kernel's appended
+        # rows (they differ from the oracle's by the fp32 rounding of the projection)
+        d["h"].copy_(torch.from_numpy(want).float())
+        Kh[:, g], Vh[:, g] = host(d["Kc"])[:, g], host(d["Vc"])[:, g]
+    assert ops.device_error() == 0
