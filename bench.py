@@ -667,6 +667,11 @@ GEMM_SHAPES = (  # name, M (= B·L rows), N, K, fp8: the attention block's proje
     ("c1_w_qkvg_b3", 1536, 4 * 768, 768, False), ("c1_w_o_b3", 1536, 768, 768, False),
     ("c2_w_qkvg_b3", 1536, 4 * 2048, 2048, False), ("c2_w_o_b3", 1536, 2048, 2048, False),
     ("c2_w_qkvg_b3_fp8", 1536, 4 * 2048, 2048, True), ("c2_w_o_b3_fp8", 1536, 2048, 2048, True),
+    # the MLP around the SwiGLU (engine/fused.py:305-310), hidden = 2.875·D as in the Small model's
+    # 1280 -> 3680 (ref/gemm_bench.py:26)
+    ("c1_w_13_b3", 1536, 2 * 2208, 768, False), ("c1_w_2_b3", 1536, 768, 2208, False),
+    ("c2_w_13_b3", 1536, 2 * 5888, 2048, False), ("c2_w_2_b3", 1536, 2048, 5888, False),
+    ("c2_w_13_b3_fp8", 1536, 2 * 5888, 2048, True), ("c2_w_2_b3_fp8", 1536, 2048, 5888, True),
 )
 
 

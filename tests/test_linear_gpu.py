@@ -41,6 +41,49 @@ def test_linear_matches_oracle(cuda, M, N, K):
     assert rel_l2(got, lib) < 3e-3
 
 
+# The MLP projections around the SwiGLU (engine/fused.py:305-310): w_13 (N = 2·hidden, K = D) and w_2
+# (N = D, K = hidden) at B·L = 1536 rows. The Small model's own widths D = 1280, hidden = 3680 (the
+# reference's GEMM bench, ref/gemm_bench.py:26), and the same hidden/D ratio at BASELINE's c1 (D = 768)
+# and c2 (D = 2048) widths.
+MLP_SHAPES = [  # name, M, N, K
+    ("small_w13", 1536, 7360, 1280), ("small_w2", 1536, 1280, 3680),
+    ("c1_w13", 1536, 4416, 768), ("c1_w2", 1536, 768, 2208),
+    ("c2_w13", 1536, 11776, 2048), ("c2_w2", 1536, 2048, 5888),
+]
+
+
+@pytest.mark.parametrize("name,M,N,K", MLP_SHAPES, ids=[s[0] for s in MLP_SHAPES])
+def test_linear_mlp_shapes(cuda, name, M, N, K):
+    """bf16 and FP8 at the MLP shapes: against torch's cuBLAS GEMM / cuBLASLt _scaled_mm on the whole
+    output, and against the float64 oracle on its first 128 rows (the oracle's full product would take
+    the CPU longer than the test is worth)."""
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).bfloat16()
+    w = (torch.randn(N, K, generator=g) * K ** -0.5).bfloat16()
+    y = ops.dit_linear(x.to(cuda), w.to(cuda))
+    lib = torch.nn.functional.linear(x.to(cuda), w.to(cuda))
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert rel_l2(y.float().cpu().numpy(), lib.float().cpu().numpy()) < 3e-3
+    want = D.linear(x[:128].float().numpy(), w.float().numpy(), "f32")
+    assert rel_l2(y[:128].float().cpu().numpy(), want) < 3e-3
+    x8, w8 = _e4m3_operands(M, N, K, M * 3 + N + K)
+    inv_x, inv_w = torch.tensor([1 / 16], device=cuda), torch.tensor([1 / 64], device=cuda)
+    xt, wt = torch.from_numpy(x8).to(cuda), torch.from_numpy(w8).to(cuda)
+    y8 = ops.dit_linear_fp8(xt, wt, inv_x, inv_w)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert rel_l2(y8[:128].float().cpu().numpy(), D.linear_fp8(x8[:128], w8, 1 / 16, 1 / 64)) < 3e-3
+    if hasattr(torch, "_scaled_mm"):
+        try:
+            lib8 = torch._scaled_mm(xt.view(torch.float8_e4m3fn), wt.view(torch.float8_e4m3fn).t(), inv_x, inv_w,
+                                    out_dtype=torch.bfloat16)
+        except RuntimeError:
+            lib8 = None
+        if lib8 is not None:
+            assert rel_l2(y8.float().cpu().numpy(), lib8.float().cpu().numpy()) < 3e-3
+
+
 @pytest.mark.parametrize("tile_n", [64, 128, 256])
 @pytest.mark.parametrize("M,N,K", [(1536, 3072, 768), (97, 200, 72), (257, 1032, 4104), (640, 136, 520)])
 def test_linear_every_tile_width(cuda, tile_n, M, N, K):
