@@ -397,6 +397,26 @@ template <>
 struct Vec4<float> {
   static __device__ __forceinline__ float4 ld(const float* p) { return *reinterpret_cast<const float4*>(p); }
 };
+template <typename CT>
+struct Vec8;  // eight consecutive cache elements from shared memory (one 16-byte load for bf16)
+template <>
+struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    v[0] = __uint_as_float(u.x << 16), v[1] = __uint_as_float(u.x & 0xffff0000u);
+    v[2] = __uint_as_float(u.y << 16), v[3] = __uint_as_float(u.y & 0xffff0000u);
+    v[4] = __uint_as_float(u.z << 16), v[5] = __uint_as_float(u.z & 0xffff0000u);
+    v[6] = __uint_as_float(u.w << 16), v[7] = __uint_as_float(u.w & 0xffff0000u);
+  }
+};
+template <>
+struct Vec8<float> {
+  static __device__ __forceinline__ void ld(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  }
+};
 
 
 constexpr int kThreadsCl = 256;  // 8 warps: two per scheduler, so dependent chains overlap
@@ -554,8 +574,63 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
   bool ok = true;
   if (n_ld > 0) ok = mbar_wait(&bar, 0, err);  // on a time-out the output is invalid (error word set)
 
-  // ---- scores, 64 keys per pass: warp w owns keys [8w, 8w+8) of the pass; lane owns 4 dims
-  {
+  // ---- scores. Up to 64 keys (T <= 1024 with clusters of 16): one pass of 8 keys per warp, lane owns
+  // 4 dims. More keys: 16 keys per warp and pass as 8 pairs, half-warp h = lane / 16 taking key 2i + h
+  // of pair i with 8 dims per lane (one 16-byte load per key for bf16), so 128 keys still take one pass
+  // — measured faster above 64 keys, slower below (twice the work per warp pass).
+  if (n > 64) {
+    const int hl = lane & 15, h = lane >> 4;
+    float qa[kG][8];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      const float4 a = *reinterpret_cast<const float4*>(&q_s[g][8 * hl]);
+      const float4 b = *reinterpret_cast<const float4*>(&q_s[g][8 * hl + 4]);
+      qa[g][0] = a.x, qa[g][1] = a.y, qa[g][2] = a.z, qa[g][3] = a.w;
+      qa[g][4] = b.x, qa[g][5] = b.y, qa[g][6] = b.z, qa[g][7] = b.w;
+    }
+    float knew[8];
+    {
+      const float4 a = *reinterpret_cast<const float4*>(&kn_s[8 * hl]);
+      const float4 b = *reinterpret_cast<const float4*>(&kn_s[8 * hl + 4]);
+      knew[0] = a.x, knew[1] = a.y, knew[2] = a.z, knew[3] = a.w;
+      knew[4] = b.x, knew[5] = b.y, knew[6] = b.z, knew[7] = b.w;
+    }
+    for (int base = 0; base < n; base += 128) {
+      float part[kG * 8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int j = base + 16 * w + 2 * i + h;
+        float k8[8];
+        if (ok && j < n_ld && SK_INB(j < chunk_max, err)) {
+          Vec8<CT>::ld(Ks + (size_t)j * kHD + 8 * hl, k8);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) k8[e] = knew[e];
+        }
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+          float acc = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc += qa[g][e] * k8[e];
+          part[g * 8 + i] = acc;
+        }
+      }
+      // reduce-scatter of 16 values over lane bits 3..0 (within each half-warp)
+#pragma unroll
+      for (int off = 8, m = 16; off >= 1; off >>= 1, m >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < m / 2; ++i) {
+          const float send = upper ? part[i] : part[i + m / 2];
+          const float keep = upper ? part[i + m / 2] : part[i];
+          part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      // lane now holds value index hl: head (hl >> 3), pair (hl & 7) -> key 16w + 2 (hl & 7) + h
+      const int g = hl >> 3, j = base + 16 * w + 2 * (hl & 7) + h;
+      if (j < n && SK_INB(j < ((chunk_max + 63) & ~63), err)) sc[j * kG + g] = part[0];
+    }
+  } else {
     float4 qa[kG];
 #pragma unroll
     for (int g = 0; g < kG; ++g) qa[g] = *reinterpret_cast<const float4*>(&q_s[g][4 * lane]);
