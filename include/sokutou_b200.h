@@ -328,8 +328,8 @@ SK_API int sk_decode_attention_block(float* h, const float* in_norm, float eps_i
 /*
  * sk_decode_attention without a workspace argument: allocates nothing, for callers that cannot call
  * cudaMalloc when they attend (a serving process that reserves its device memory up front and
- * forbids allocation afterwards, a driver running inside a CUDA graph capture, a foreign-language
- * binding that only passes buffers it already owns). No counterpart in the reference: its kernel
+ * forbids allocation afterwards, a foreign-language binding that only passes buffers it already
+ * owns and has no allocator of its own). No counterpart in the reference: its kernel
  * (qwen3/kernels.py:338-414) keeps all scores in shared memory and needs no scratch.
  *
  * Same arguments and results as sk_decode_attention. The split-KV scratch is a 1 MiB array inside

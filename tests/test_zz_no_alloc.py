@@ -1,7 +1,7 @@
 """sk_decode_attention_noalloc — the decode attention for callers that cannot allocate device memory
-when they attend (a serving process that reserves its device memory at start-up, a driver inside a
-CUDA graph capture, a foreign-language binding that only passes buffers it owns). It keeps its
-split-KV scratch in a fixed array inside the library instead of a caller workspace.
+when they attend (a serving process that reserves its device memory at start-up, a foreign-language
+binding that only passes buffers it owns). It keeps its split-KV scratch in a fixed array inside the
+library instead of a caller workspace.
 
 Checked through the C ABI against sk_decode_attention on identical inputs and against the float64
 oracle, two calls in a row with different cache lengths (so the second call reuses the scratch the
