@@ -15,8 +15,12 @@
  *
  * Conventions
  *   - Every entry point returns an int status: SK_OK (0) or a negative SK_ERR_* code. Nothing aborts.
- *   - Pointers are raw device pointers of contiguous buffers owned by the caller; the kernels allocate
- *     nothing, so every call may be captured into a CUDA graph once the caller's buffers exist.
+ *   - Pointers are raw device pointers of contiguous buffers owned by the caller, and the kernels
+ *     allocate nothing (sk_decode_attention_noalloc keeps its scratch in a fixed array of its own).
+ *     The DiT, gate, projection, prefill, decode, decode-block and grouped-decode entry points launch
+ *     kernels only, so their calls can be captured into a CUDA graph once the caller's buffers exist
+ *     (graph-replay tests cover the DiT attention and fused block, the projections, the decode, the
+ *     decode block and grouped decode).
  *   - `stream` is a cudaStream_t passed as void* so that this header needs no CUDA include.
  *   - Launches are asynchronous. A device-side failure (an invalid position read from device memory,
  *     a bounded wait that ran out) is recorded in a per-device error word; read it with
