@@ -164,3 +164,16 @@ def talker_greedy(weights: dict, n_layers: int, nq: int, nkv: int, hd: int, max_
             tok = int(np.argmax(w["w_out"] @ rms(h)))
             tokens.append(tok)
     return tokens
+
+
+def decode_block_pair(h2, in_norm, eps_in: float, w_qkv, qn, kn, eps: float, rope, Kc, Vc, nq: int, nkv: int, w_o,
+                      cache_dtype: str = "bf16"):
+    """The attention half of the code predictor's paired pass over positions 0 and 1
+    (qwen3/kernels.py:600-617, `_cp_layers_pair`): `rms_gemv2` projects both rows first (each row's own
+    RMSNorm), then `attn` runs position 0 (appending its k/v at row 0 of the 16-row cache) and then
+    position 1 (appending at row 1 and attending over rows 0..1), then `gemv2` adds W_o · att to both
+    residual rows. Mutates Kc/Vc; returns the two new rows of h (float64). (The reference skips row 0's
+    o projection in the stack's last layer; that choice sits outside the attention block.)"""
+    qkv = [rms_gemv(h2[r], in_norm, eps_in, w_qkv) for r in (0, 1)]
+    att = [decode_step(qkv[r], qn, kn, eps, rope, Kc, Vc, r, nq, nkv, cache_dtype) for r in (0, 1)]
+    return [gemv_acc(att[r], w_o, h2[r]) for r in (0, 1)]

@@ -226,3 +226,34 @@ def test_code_predictor_form_positions_from_pos_add(cuda, wdt, cdt):
         d["h"].copy_(torch.from_numpy(want).float())
         Kh[:, g], Vh[:, g] = host(d["Kc"])[:, g], host(d["Vc"])[:, g]
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("wdt,cdt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16)])
+def test_code_predictor_pair_as_two_launches(cuda, wdt, cdt):
+    """The code predictor's paired pass (qwen3/kernels.py:600-617: both rows projected, then attention at
+    position 0 and at position 1, then the o projection of both rows) is the same arithmetic as two block
+    launches in a row — row 0 at pos_add 0, then row 1 at pos_add 1 — because row 1's projection reads
+    only its own residual row: against the oracle's restatement of the paired pass, with each row's h
+    and the two appended cache rows."""
+    max_len, hidden = 16, 1024
+    d = _case(cuda, hidden, max_len, 1, wdt, cdt, seed=47)
+    d["Kc"].zero_()
+    d["Vc"].zero_()
+    g = torch.Generator().manual_seed(48)
+    h2 = torch.randn(2, hidden, generator=g).to(cuda)
+    Kh, Vh = host(d["Kc"]), host(d["Vc"])
+    want = Q.decode_block_pair(host(h2), host(d["in_norm"]), 1e-6, host(d["w_qkv"]), host(d["qn"]), host(d["kn"]),
+                               1e-6, d["rope"].cpu().numpy(), Kh, Vh, 16, 8, host(d["w_o"]),
+                               "bf16" if cdt == torch.bfloat16 else "f32")
+    ws = ops.decode_block_workspace(max_len, 16, 8, cuda)
+    rows = [h2[0].clone(), h2[1].clone()]
+    for r in (0, 1):
+        ops.decode_attention_block(rows[r], d["in_norm"], 1e-6, d["w_qkv"], d["qn"], d["kn"], 1e-6, d["rope"], d["Kc"],
+                                   d["Vc"], None, r, max_len, 16, 8, d["w_o"], ws)
+    torch.cuda.synchronize()
+    tol = FP32_TOL if (wdt, cdt) == (torch.float32, torch.float32) else BF16_TOL
+    for r in (0, 1):
+        assert rel_l2(host(rows[r]), want[r]) <= tol, r
+        assert rel_l2(host(d["Kc"])[:, r], Kh[:, r]) <= tol and rel_l2(host(d["Vc"])[:, r], Vh[:, r]) <= tol
+    assert torch.all(d["Kc"][:, 2:] == 0) and torch.all(d["Vc"][:, 2:] == 0)
+    assert ops.device_error() == 0

@@ -71,3 +71,25 @@ def test_profile_module_runs_as_a_script():
     r = subprocess.run([sys.executable, "-m", "sokutou_b200.profile", "--help"], cwd=root, capture_output=True,
                        text=True, timeout=300)
     assert r.returncode == 0 and "--case" in r.stdout
+
+
+def test_code_predictor_pair_equals_two_sequential_blocks():
+    """The oracle's paired code-predictor pass (qwen3/kernels.py:600-617) and two single-position blocks
+    in a row (positions 0 then 1) are the same float64 arithmetic: row 1's projection reads only its own
+    residual row, and its attention sees row 0's appended key either way."""
+    import numpy as np
+    from oracle import decode_attn_ref as Q
+    rng = np.random.default_rng(0)
+    hid, nq, nkv, hd = 256, 16, 8, 128
+    W = rng.standard_normal(((nq + 2 * nkv) * hd, hid)) / 16
+    Wo = rng.standard_normal((hid, nq * hd)) / 45
+    nw, ones = 1 + 0.1 * rng.standard_normal(hid), np.ones(hd)
+    rope, h2 = Q.rope_table(16), rng.standard_normal((2, hid))
+    K1, V1 = np.zeros((nkv, 16, hd)), np.zeros((nkv, 16, hd))
+    K2, V2 = K1.copy(), V1.copy()
+    a = Q.decode_block_pair(h2, nw, 1e-6, W, ones, ones, 1e-6, rope, K1, V1, nq, nkv, Wo, "f32")
+    b = [Q.decode_block(h2[r], nw, 1e-6, W, ones, ones, 1e-6, rope, K2, V2, r, nq, nkv, Wo, "f32") for r in (0, 1)]
+    for r in (0, 1):
+        np.testing.assert_array_equal(a[r], b[r])
+    np.testing.assert_array_equal(K1, K2)
+    np.testing.assert_array_equal(V1, V2)
