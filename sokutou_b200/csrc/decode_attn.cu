@@ -422,8 +422,31 @@ struct Vec8<float> {
 constexpr int kThreadsCl = 256;  // 8 warps: two per scheduler, so dependent chains overlap
 constexpr int kPartialBytes = kG * kHD * 4 + kG * 2 * 4;  // one CTA's (o, max, sum) for rank 0
 
+// Rows of the K region of a cluster CTA: its chunk and, in the compact layout, at least the 8 warps'
+// PV partials (8 · kG · kHD floats), which reuse that region once the scores are done.
+template <typename CT>
+__host__ __device__ constexpr int k_rows(int chunk_max, bool compact) {
+  return compact && chunk_max < 8 * kG * 4 / (int)sizeof(CT) ? 8 * kG * 4 / (int)sizeof(CT) : chunk_max;
+}
+
+// Dynamic shared memory of a cluster CTA, in the order the kernel lays it out: K region, V chunk,
+// scores (kG per key, padded to 64 keys) and, in the compact layout, rank 0's CL partial o. 0 when
+// the K/V chunks and scores of ceil(max_len / cl) keys exceed 160 KB.
+// The compact layout (grouped launches) keeps the PV partials and rank 0's partials in dynamic
+// memory sized by the cluster, 2.5 KB of static memory instead of 26.5 KB, so more CTAs fit on an
+// SM when many clusters queue; a single launch (nkv clusters, one CTA per SM) keeps the static
+// arrays, measured ~5 % faster there (T = 1120: 4.95 vs 5.20 us).
+template <typename CT>
+static size_t cluster_smem(int max_len, int cl, bool compact) {
+  const int chunk_max = (max_len + cl - 1) / cl;
+  const size_t chunks = 2 * (size_t)chunk_max * kHD * sizeof(CT) + (size_t)kG * ((chunk_max + 63) & ~63) * 4;
+  if (chunks > 160 * 1024) return 0;
+  if (!compact) return chunks;
+  return chunks + (size_t)(k_rows<CT>(chunk_max, true) - chunk_max) * kHD * sizeof(CT) + (size_t)cl * kG * kHD * 4;
+}
+
 // Cluster variant: one thread-block cluster of CL CTAs per kv head, CL = 16 (or 8 where 16 cannot
-// be co-scheduled). The T keys are cut into CL equal chunks of ceil(T / CL) keys, so every CTA is
+// be co-scheduled; grouped launches choose by residency, below). The T keys are cut into CL equal chunks of ceil(T / CL) keys, so every CTA is
 // busy at every T. Each CTA pushes its chunk's partial (o, max, sum) into rank 0's shared memory
 // with st.async, whose completion is counted in bytes on rank 0's mbarrier; rank 0 waits for all
 // CL partials and merges them from its own shared memory. No workspace, no global round trip, no
@@ -469,15 +492,22 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
   const int CL = (int)cluster_size_reg();
   const int rank = (int)cluster_rank();
   const int chunk_max = (max_len + CL - 1) / CL;
+  const int chunk_pad = (chunk_max + 63) & ~63;
   extern __shared__ __align__(128) unsigned char dsmem[];
-  CT* Ks = reinterpret_cast<CT*>(dsmem);                               // [chunk_max][kHD]
-  CT* Vs = Ks + (size_t)chunk_max * kHD;                               // [chunk_max][kHD]
+  CT* Ks = reinterpret_cast<CT*>(dsmem);                               // [k_rows][kHD]
+  CT* Vs = Ks + (size_t)k_rows<CT>(chunk_max, GROUPED) * kHD;          // [chunk_max][kHD]
   float* sc = reinterpret_cast<float*>(Vs + (size_t)chunk_max * kHD);  // [chunk_pad][kG]: scores, then p
+  // PV partials of the 8 key groups [8][kG][kHD], and rank 0's copy of every CTA's chunk partial o
+  // [CL][kG][kHD]: static arrays for a single launch; in the compact layout (GROUPED) the first lies
+  // over the K chunk (read only by the scores, which are done when the PV pass writes it) and the
+  // second follows the scores (the unused static arrays are dropped from that instantiation)
+  __shared__ __align__(16) float o_red_s[8][kG][kHD];
+  __shared__ __align__(16) float all_o_s[kMaxCluster][kG][kHD];
+  float(*o_red)[kG][kHD] = GROUPED ? reinterpret_cast<float(*)[kG][kHD]>(dsmem) : o_red_s;
+  float(*all_o)[kG][kHD] = GROUPED ? reinterpret_cast<float(*)[kG][kHD]>(sc + (size_t)chunk_pad * kG) : all_o_s;
   __shared__ __align__(16) float q_s[kG][kHD];
   __shared__ __align__(16) float kn_s[kHD];
   __shared__ __align__(16) float vn_s[kHD];
-  __shared__ __align__(16) float o_red[8][kG][kHD];            // PV partials of the 8 key groups
-  __shared__ __align__(16) float all_o[kMaxCluster][kG][kHD];  // rank 0: every CTA's chunk partial o
   __shared__ __align__(16) float all_ml[kMaxCluster][kG][2];   // rank 0: every CTA's chunk (max, sum)
   __shared__ float wts[kMaxCluster][kG];                       // rank 0: merge weights
   __shared__ float den_s[kG];
@@ -628,7 +658,7 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
       }
       // lane now holds value index hl: head (hl >> 3), pair (hl & 7) -> key 16w + 2 (hl & 7) + h
       const int g = hl >> 3, j = base + 16 * w + 2 * (hl & 7) + h;
-      if (j < n && SK_INB(j < ((chunk_max + 63) & ~63), err)) sc[j * kG + g] = part[0];
+      if (j < n && SK_INB(j < chunk_pad, err)) sc[j * kG + g] = part[0];
     }
   } else {
     float4 qa[kG];
@@ -660,7 +690,7 @@ __global__ void __launch_bounds__(kThreadsCl) decode_attn_cluster_kernel(
       part[0] += __shfl_xor_sync(0xffffffffu, part[0], 1);
       // lane l now holds value index (l >> 1): head (l >> 4), key (l >> 1) & 7
       const int g = lane >> 4, j = base + 8 * w + ((lane >> 1) & 7);
-      if ((lane & 1) == 0 && j < n && SK_INB(j < ((chunk_max + 63) & ~63), err)) sc[j * kG + g] = part[0];
+      if ((lane & 1) == 0 && j < n && SK_INB(j < chunk_pad, err)) sc[j * kG + g] = part[0];
     }
   }
   __syncthreads();
@@ -862,9 +892,8 @@ static int launch_cluster(const float* qkv, const float* qn, const float* kn, fl
                           int* err, bool early, cudaStream_t st) {
   // the shared memory of the largest chunk decides whether one cluster per kv head can hold T = max_len
   for (int cl : {16, 8}) {
-    const int chunk_max = (max_len + cl - 1) / cl;
-    const size_t smem = 2 * (size_t)chunk_max * kHD * sizeof(CT) + (size_t)kG * ((chunk_max + 63) & ~63) * 4;
-    if (smem > 160 * 1024) continue;
+    const size_t smem = cluster_smem<CT>(max_len, cl, false);
+    if (smem == 0) continue;
     const int use = cluster_size<CT>(nkv, smem);
     if (use != cl) continue;
     cudaLaunchConfig_t cfg = {};
@@ -894,72 +923,91 @@ static int launch_cluster(const float* qkv, const float* qn, const float* kn, fl
   return SK_ERR_UNSUPPORTED;
 }
 
+// Clusters of `cl` CTAs of a grouped launch that can be resident on the device at once (0 when none).
+template <typename CT>
+static int grouped_clusters(void (*kern)(const float*, const float*, const float*, float, const float*, CT*, CT*,
+                                         const long long*, int, int, int, int, float*, int*, const SkDecodeRequest*),
+                            int cl, int nkv, size_t smem) {
+  cudaLaunchConfig_t q = {};
+  q.gridDim = dim3(cl, nkv);
+  q.blockDim = dim3(kThreadsCl);
+  q.dynamicSmemBytes = smem;
+  cudaLaunchAttribute a[1];
+  a[0].id = cudaLaunchAttributeClusterDimension;
+  a[0].val.clusterDim.x = cl;
+  a[0].val.clusterDim.y = 1;
+  a[0].val.clusterDim.z = 1;
+  q.attrs = a;
+  q.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess) {
+    cudaGetLastError();  // clear a refused query
+    return 0;
+  }
+  return n;
+}
+
+// The clusters of a grouped launch depend on nothing outside themselves and may run wave after wave.
+// Cluster size: 8 when strictly more clusters of 8 than of 16 are resident at once (the same number of
+// clusters, nkv · R, then runs in fewer waves, and each request's partials merge over 8 CTAs instead of
+// 16), else 16; whichever of the two is schedulable when only one is. Decided once per device, mode and
+// max_len. Measured at T = 1120, bf16, R = 8 / 16 / 32: max_len 1536 (a CTA of a 16-cluster holds 70 KB
+// of shared memory, one of an 8-cluster 112 KB: 3 and 2 per SM) 19.2 / 33.7 / 62.2 us with 16,
+// 17.6 / 29.2 / 51.9 us with 8; max_len 1152 (57 KB and 87 KB: 4 and 2 per SM) 17.3 / 29.1 / 52.4 vs
+// 17.4 / 29.0 / 52.1 us.
 template <typename CT>
 static int launch_grouped(const SkDecodeRequest* reqs, int R, int max_len, int nq, int nkv, int* err, bool early,
                           cudaStream_t st) {
-  for (int cl : {16, 8}) {
-    const int chunk_max = (max_len + cl - 1) / cl;
-    const size_t smem = 2 * (size_t)chunk_max * kHD * sizeof(CT) + (size_t)kG * ((chunk_max + 63) & ~63) * 4;
-    if (smem > 160 * 1024) continue;
-    auto kern = early ? decode_attn_cluster_kernel<CT, true, true> : decode_attn_cluster_kernel<CT, false, true>;
-    cudaLaunchConfig_t cfg = {};
-    {
-      // the clusters of a grouped launch depend on nothing outside themselves: they may run wave after
-      // wave, so one schedulable cluster of this size is enough (cached per device, mode and size)
-      static std::mutex mu;
-      static size_t set_to[64][2] = {};
-      static int ok_cl[64][2] = {};
-      static size_t ok_smem[64][2] = {};
-      int dev = 0;
-      if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SK_ERR_CUDA;
-      std::lock_guard<std::mutex> lk(mu);
-      if (set_to[dev][early] < smem) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  auto kern = early ? decode_attn_cluster_kernel<CT, true, true> : decode_attn_cluster_kernel<CT, false, true>;
+  int cl = 0;
+  size_t smem = 0;
+  {
+    static std::mutex mu;
+    static size_t set_to[64][2] = {};
+    static int for_len[64][2] = {};
+    static int chosen[64][2] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SK_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(mu);
+    if (for_len[dev][early] != max_len || chosen[dev][early] == 0) {
+      const size_t s16 = cluster_smem<CT>(max_len, 16, true), s8 = cluster_smem<CT>(max_len, 8, true);
+      const size_t top = s16 > s8 ? s16 : s8;
+      if (top == 0) return SK_ERR_UNSUPPORTED;
+      if (set_to[dev][early] < top) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)top) != cudaSuccess)
           return SK_ERR_CUDA;
         cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        set_to[dev][early] = smem;
+        set_to[dev][early] = top;
       }
-      if (ok_smem[dev][early] != smem || ok_cl[dev][early] != cl) {
-        cudaLaunchConfig_t q = {};
-        q.gridDim = dim3(cl, nkv);
-        q.blockDim = dim3(kThreadsCl);
-        q.dynamicSmemBytes = smem;
-        cudaLaunchAttribute a[1];
-        a[0].id = cudaLaunchAttributeClusterDimension;
-        a[0].val.clusterDim.x = cl;
-        a[0].val.clusterDim.y = 1;
-        a[0].val.clusterDim.z = 1;
-        q.attrs = a;
-        q.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n < 1) {
-          cudaGetLastError();  // clear a refused query
-          continue;
-        }
-        ok_cl[dev][early] = cl;
-        ok_smem[dev][early] = smem;
-      }
+      const int n16 = s16 ? grouped_clusters<CT>(kern, 16, nkv, s16) : 0;
+      const int n8 = s8 ? grouped_clusters<CT>(kern, 8, nkv, s8) : 0;
+      const int pick = n8 > n16 ? 8 : (n16 > 0 ? 16 : 0);
+      if (pick == 0) return SK_ERR_UNSUPPORTED;
+      chosen[dev][early] = pick;
+      for_len[dev][early] = max_len;
     }
-    cfg.gridDim = dim3(cl, nkv, R);
-    cfg.blockDim = dim3(kThreadsCl);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cl;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    if (cudaLaunchKernelEx(&cfg, kern, (const float*)nullptr, (const float*)nullptr, (const float*)nullptr, 0.f,
-                           (const float*)nullptr, (CT*)nullptr, (CT*)nullptr, (const long long*)nullptr, 0, max_len,
-                           nq, nkv, (float*)nullptr, err, reqs) != cudaSuccess)
-      return SK_ERR_CUDA;
-    return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
+    cl = chosen[dev][early];
+    smem = cluster_smem<CT>(max_len, cl, true);
   }
-  return SK_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cl, nkv, R);
+  cfg.blockDim = dim3(kThreadsCl);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (cudaLaunchKernelEx(&cfg, kern, (const float*)nullptr, (const float*)nullptr, (const float*)nullptr, 0.f,
+                         (const float*)nullptr, (CT*)nullptr, (CT*)nullptr, (const long long*)nullptr, 0, max_len, nq,
+                         nkv, (float*)nullptr, err, reqs) != cudaSuccess)
+    return SK_ERR_CUDA;
+  return cudaPeekAtLastError() == cudaSuccess ? SK_OK : SK_ERR_CUDA;
 }
 
 }  // namespace decode

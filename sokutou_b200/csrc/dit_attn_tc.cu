@@ -220,8 +220,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const int bc = prm.ctx_batched ? b : 0;
       // latent tiles: (column, row, batch·head) of (B·H, L, hd) buffers; the fused block's v (and gate)
       // tiles are (column, row, batch) of o4 at column offset 2·D (3·D) plus the head's h·hd
-      // q: (b, h); k and v: the (b, h / kv_group) head of the key/value buffers
-      const int lz = b * prm.H + h, lzk = b * (prm.H / prm.kv_group) + h / prm.kv_group, lzv = VO4 ? b : lzk;
+      // k and v: the (b, h / kv_group) head of the key/value buffers (q went out after the wait)
+      const int lzk = b * (prm.H / prm.kv_group) + h / prm.kv_group, lzv = VO4 ? b : lzk;
       const int xv = VO4 ? 2 * prm.D + h * HD : 0;
       if (FUSED) {  // the gate tile is loaded after the last S = Q·Kᵀ; start its trip to L2 now
 #pragma unroll
