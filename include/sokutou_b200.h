@@ -285,8 +285,9 @@ typedef struct SkDecodeRequest {
 /*
  * R independent decode requests in one launch: request r does what sk_decode_attention does with the
  * arguments in reqs[r] — the same appended cache rows, and the output of its thread-block-cluster kernel
- * (the same bits where sk_decode_attention runs that kernel too; within rounding where it falls back
- * to its split-KV workspace kernel) — all sharing max_len, nq, nkv, hd and the cache dtype. No counterpart in the reference, which serves one request at a time (README.md:186): a server
+ * (the same bits where sk_decode_attention runs that kernel with the same cluster size; within rounding
+ * otherwise: the grouped launch takes clusters of 8 where more of them than of 16 are resident at once,
+ * and the chunk split sets the merge order) — all sharing max_len, nq, nkv, hd and the cache dtype. No counterpart in the reference, which serves one request at a time (README.md:186): a server
  * holding several talkers' decodes in flight gets one launch per layer for all of them instead of one
  * per request, and so moves R times the cache bytes per launch.
  *   reqs  : DEVICE pointer to R descriptors (filled before capture; they are read on the device)
