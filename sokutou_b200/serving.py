@@ -286,9 +286,8 @@ class GpuExecutor:
     # (sk_decode_attention_grouped): every step advances every slot by one position; a slot whose
     # request has reached its final length takes the next waiting request (its position reset to the
     # prompt length). Requests are handed out longest first, so the slots finish close together.
-    # 16 slots measured best for c4 on one B200 with 16-CTA grouped clusters (34.7 sentences/s vs 32.9
-    # with 8; 20.5 with 32, whose idle slots keep launching through the tail); 55.5 sentences/s with
-    # the compact grouped layout and clusters of 8.
+    # 16 slots measured best for c4 on one B200: 55.3 sentences/s against 50.2 with 8, 52.0 with 12,
+    # 51.8 with 20, 43.8 with 24 and 33.2 with 32 (idle slots keep launching through the tail).
     SLOTS = 16
 
     def _decode_slots(self):
